@@ -1,0 +1,209 @@
+// Row-wise kernels: token embedding gather, RMSNorm (optionally fused with the residual
+// add), and fused rotate-half RoPE + paged KV append.
+//
+// Reference sites: embedding (src/model/custom_transformer.rs:461), RMSNorm and fused
+// add+RMSNorm via candle-layer-norm (src/model/fused_rmsnorm.rs:47-110, block usage
+// src/model/custom_transformer_block.rs:329,348), RoPE (src/model/custom_attention.rs:687-728,
+// tables src/model/custom_transformer.rs:403-438) and the KV append gather/where/scatter
+// (src/cache/parallel_cache_builder.rs:128-185).  Here RoPE uses per-row positions (the
+// reference shares one index_pos across a decode batch, custom_transformer.rs:512-520) and
+// the rotated K / V are written straight into their paged slots in the same pass.
+#include <ATen/cuda/CUDAContext.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace lb {
+
+// ---------------------------------------------------------------------------------------
+// Embedding: out[t, :] = table[ids[t], :]
+// ---------------------------------------------------------------------------------------
+__global__ void embed_kernel(const int* ids, const bf16* table, bf16* out, int hidden,
+                             int vocab, int* err) {
+  const int t = blockIdx.x;
+  int id = ids[t];
+  if (id < 0 || id >= vocab) {
+    if (threadIdx.x == 0) record_error(err, kErrBounds);
+    id = 0;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(table + static_cast<size_t>(id) * hidden);
+  uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * hidden);
+  for (int i = threadIdx.x; i < hidden / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+// ---------------------------------------------------------------------------------------
+// RMSNorm.  If `residual` is given: residual <- residual + x (rounded to bf16 once), and
+// y = norm(residual) * w.  Otherwise y = norm(x) * w.  One CTA per row, 16-byte vectors.
+// ---------------------------------------------------------------------------------------
+template <int VPT>
+__global__ void rmsnorm_kernel(const bf16* x, int ldx, bf16* residual, int ldr, const bf16* w,
+                               bf16* y, int ldy, int hidden, float eps) {
+  const int row = blockIdx.x;
+  const int nvec = hidden / 8;
+  float v[VPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int vi = threadIdx.x + i * blockDim.x;
+    if (vi < nvec) {
+      uint4 raw = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * ldx)[vi];
+      const bf16* e = reinterpret_cast<const bf16*>(&raw);
+      if (residual != nullptr) {
+        uint4 rr = reinterpret_cast<const uint4*>(residual + static_cast<size_t>(row) * ldr)[vi];
+        const bf16* re = reinterpret_cast<const bf16*>(&rr);
+        uint4 outv;
+        bf16* oe = reinterpret_cast<bf16*>(&outv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const bf16 s = __float2bfloat16(__bfloat162float(e[j]) + __bfloat162float(re[j]));
+          oe[j] = s;
+          v[i][j] = __bfloat162float(s);
+        }
+        reinterpret_cast<uint4*>(residual + static_cast<size_t>(row) * ldr)[vi] = outv;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = __bfloat162float(e[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+    }
+  }
+  __shared__ float red[32];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float inv = rsqrtf(red[0] / hidden + eps);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int vi = threadIdx.x + i * blockDim.x;
+    if (vi < nvec) {
+      uint4 wr = reinterpret_cast<const uint4*>(w)[vi];
+      const bf16* we = reinterpret_cast<const bf16*>(&wr);
+      uint4 outv;
+      bf16* oe = reinterpret_cast<bf16*>(&outv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) oe[j] = __float2bfloat16(v[i][j] * inv * __bfloat162float(we[j]));
+      reinterpret_cast<uint4*>(y + static_cast<size_t>(row) * ldy)[vi] = outv;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// RoPE + KV append.  qkv: [T, (Hq + 2 Hkv) * D] (q rotated in place).  cos_sin: [P, D]
+// fp32 (first D/2 = cos, next D/2 = sin).  slot[t] = block * BS + offset (int32, < 0: skip).
+// Cache: [num_blocks, Hkv, BS, D].
+// ---------------------------------------------------------------------------------------
+__global__ void rope_kv_kernel(bf16* qkv, int ld, const int* positions, const int* slots,
+                               const float* cos_sin, int max_pos, bf16* k_cache, bf16* v_cache,
+                               int hq, int hkv, int head_dim, int block_size, int* err) {
+  const int t = blockIdx.x;
+  int pos = positions[t];
+  if (pos < 0 || pos >= max_pos) {
+    if (threadIdx.x == 0) record_error(err, kErrBounds);
+    pos = 0;
+  }
+  const int half = head_dim / 2;
+  const float* cs = cos_sin + static_cast<size_t>(pos) * head_dim;
+  bf16* row = qkv + static_cast<size_t>(t) * ld;
+  const int64_t slot = slots != nullptr ? static_cast<int64_t>(slots[t]) : -1;
+  const int64_t blk = slot >= 0 ? slot / block_size : 0;
+  const int off = slot >= 0 ? static_cast<int>(slot % block_size) : 0;
+  // rotate q and k heads: each thread handles one (head, i) pair for i < half.
+  const int nrot = (hq + hkv) * half;
+  for (int idx = threadIdx.x; idx < nrot; idx += blockDim.x) {
+    const int h = idx / half, i = idx % half;
+    bf16* base = row + h * head_dim;
+    const float x1 = __bfloat162float(base[i]);
+    const float x2 = __bfloat162float(base[i + half]);
+    const float c = cs[i], s = cs[half + i];
+    const bf16 r1 = __float2bfloat16(x1 * c - x2 * s);
+    const bf16 r2 = __float2bfloat16(x1 * s + x2 * c);
+    if (h < hq) {
+      base[i] = r1;
+      base[i + half] = r2;
+    } else if (slot >= 0) {
+      const int kh = h - hq;
+      bf16* dst = k_cache + ((blk * hkv + kh) * block_size + off) * head_dim;
+      dst[i] = r1;
+      dst[i + half] = r2;
+    }
+  }
+  if (slot >= 0) {
+    const bf16* vsrc = row + (hq + hkv) * head_dim;
+    const int nv = hkv * head_dim / 8;
+    for (int idx = threadIdx.x; idx < nv; idx += blockDim.x) {
+      const int kh = (idx * 8) / head_dim, d = (idx * 8) % head_dim;
+      bf16* dst = v_cache + ((blk * hkv + kh) * block_size + off) * head_dim + d;
+      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(vsrc + idx * 8);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Host wrappers
+// ---------------------------------------------------------------------------------------
+void embedding(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, at::Tensor& err) {
+  const int T = ids.size(0);
+  if (T == 0) return;
+  const int hidden = table.size(1);
+  TORCH_CHECK(hidden % 8 == 0 && table.is_contiguous() && out.is_contiguous(), "embedding");
+  embed_kernel<<<T, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+      ids.data_ptr<int>(), reinterpret_cast<const bf16*>(table.data_ptr()),
+      reinterpret_cast<bf16*>(out.data_ptr()), hidden, table.size(0), err.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w,
+             at::Tensor& y, double eps) {
+  const int T = x.size(0), H = x.size(1);
+  if (T == 0) return;
+  TORCH_CHECK(H % 8 == 0 && x.stride(1) == 1 && y.stride(1) == 1, "rmsnorm layout");
+  bf16* res = nullptr;
+  int ldr = 0;
+  if (residual.has_value() && residual->defined()) {
+    res = reinterpret_cast<bf16*>(residual->data_ptr());
+    ldr = residual->stride(0);
+  }
+  const int threads = 128;
+  const int vpt = (H / 8 + threads - 1) / threads;
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  auto xp = reinterpret_cast<const bf16*>(x.data_ptr());
+  auto wp = reinterpret_cast<const bf16*>(w.data_ptr());
+  auto yp = reinterpret_cast<bf16*>(y.data_ptr());
+#define LB_RMS(V)                                                                          \
+  rmsnorm_kernel<V><<<T, threads, 0, st>>>(xp, x.stride(0), res, ldr, wp, yp, y.stride(0), H, \
+                                           static_cast<float>(eps))
+  if (vpt <= 1) LB_RMS(1);
+  else if (vpt <= 2) LB_RMS(2);
+  else if (vpt <= 4) LB_RMS(4);
+  else if (vpt <= 8) LB_RMS(8);
+  else TORCH_CHECK(false, "rmsnorm: hidden too large");
+#undef LB_RMS
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void rope_kv(at::Tensor& qkv, const at::Tensor& positions, const c10::optional<at::Tensor>& slots,
+             const at::Tensor& cos_sin, at::Tensor& k_cache, at::Tensor& v_cache, int64_t hq,
+             int64_t hkv, at::Tensor& err) {
+  const int T = qkv.size(0);
+  if (T == 0) return;
+  const int D = cos_sin.size(1);
+  TORCH_CHECK(qkv.stride(1) == 1 && qkv.size(1) >= (hq + 2 * hkv) * D, "rope_kv: qkv layout");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous(), "cos_sin f32");
+  const int* sp = nullptr;
+  if (slots.has_value() && slots->defined()) sp = slots->data_ptr<int>();
+  rope_kv_kernel<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<bf16*>(qkv.data_ptr()), qkv.stride(0), positions.data_ptr<int>(), sp,
+      cos_sin.data_ptr<float>(), cos_sin.size(0), reinterpret_cast<bf16*>(k_cache.data_ptr()),
+      reinterpret_cast<bf16*>(v_cache.data_ptr()), hq, hkv, D, k_cache.size(2),
+      err.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace lb

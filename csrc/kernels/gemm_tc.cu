@@ -1,0 +1,550 @@
+// Dense bf16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA), sm_100a.
+//
+//   C[M, N] = A[M, K] . W[N, K]^T   (+ residual)   with fused epilogues
+//
+// Replaces every `Linear` of the reference (cuBLAS through candle, e.g. the q/k/v/o
+// projections at src/model/custom_attention.rs:265-267,671 and the MLP at
+// src/model/mlp_wrapper.rs:185-195).
+//
+// Design (B200-first):
+//  * "swap-AB": the weight tile is the MMA's 128-row A operand and the token tile is the
+//    MMA's N dimension (16..256).  Decode batches of a few tokens then still issue full
+//    128-row MMAs and weights are streamed exactly once.
+//  * persistent CTAs (one per SM), warp-specialised: warp 0 issues TMA loads into a
+//    STAGES-deep shared-memory ring, warp 1 (one thread) issues tcgen05.mma into a
+//    double-buffered TMEM accumulator, warps 2..5 drain TMEM with tcgen05.ld and run the
+//    epilogue while the next tile's MMAs proceed.
+//  * split-K for small tile counts: fp32 partial tiles go to a workspace, the last CTA to
+//    arrive on the tile's counter reduces them in fixed split order (deterministic) and
+//    resets the counter for the next launch.
+//  * epilogues: bf16 store (+ residual add), fp32 store (logits), and SwiGLU on
+//    gate/up rows interleaved in 64-row groups (writes silu(g) * u, half width).
+//  * no cluster multicast: every TMA load reads this GPU's own memory.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cudaTypedefs.h>
+#include <torch/extension.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace lb {
+
+constexpr int BW = 128;        // weight rows per tile (MMA M)
+constexpr int BK = 64;         // K elements per pipeline stage (one 128-byte swizzle row)
+constexpr int UK = 16;         // K per tcgen05.mma kind::f16
+constexpr int kThreads = 192;  // warp 0: TMA, warp 1: MMA, warps 2..5: epilogue
+
+enum EpiMode : int { kEpiStore = 0, kEpiSwiGLU = 1, kEpiF32 = 2 };
+
+struct GemmArgs {
+  int M, N, K;
+  int m_tiles, n_tiles, splits, kb_per_split, kb_total;
+  void* C;
+  int ldc;
+  const bf16* residual;
+  int ldr;
+  float* ws;
+  int* counters;
+  int mode;
+  int* err;
+};
+
+template <int BT, int STAGES>
+struct GemmSmem {
+  static constexpr int W_BYTES = BW * BK * 2;
+  static constexpr int X_BYTES = BT * BK * 2;
+  static constexpr int CH = BT < 32 ? BT : 32;  // epilogue column chunk
+  static constexpr int EPI_FLOATS = 64 * (CH + 1);
+  static constexpr int BAR_OFF = STAGES * (W_BYTES + X_BYTES) + EPI_FLOATS * 4;
+  static constexpr int TOTAL = BAR_OFF + 256 + 1024;  // barriers/flags + alignment slack
+  static constexpr int TMEM_COLS = 2 * BT < 32 ? 32 : 2 * BT;
+};
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+
+template <int BT, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                   const GemmArgs a) {
+  using L = GemmSmem<BT, STAGES>;
+  constexpr int CH = L::CH;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sW = smem;
+  uint8_t* sX = smem + STAGES * L::W_BYTES;
+  float* sEpi = reinterpret_cast<float*>(sX + STAGES * L::X_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* s_last = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  volatile int* s_go = reinterpret_cast<volatile int*>(tmem_slot + 4);  // [2]
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmW);
+    prefetch_tmap(&tmX);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, L::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total = a.m_tiles * a.n_tiles * a.splits;
+  // unit -> (m tile, n tile, split); consecutive units share the token tile so that the
+  // activation stays in L2 while each weight tile is streamed once.
+  auto decode_unit = [&](int u, int& mt, int& nt, int& s) {
+    s = u % a.splits;
+    int t = u / a.splits;
+    nt = t % a.n_tiles;
+    mt = t / a.n_tiles;
+  };
+
+  uint32_t issued_mask = 0, issued_parity = 0;  // producer bookkeeping for abort drain
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pw = policy_evict_first();
+      const uint64_t px = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
+        int mt, nt, s;
+        decode_unit(u, mt, nt, s);
+        const int kb0 = s * a.kb_per_split;
+        const int kb1 = min(kb0 + a.kb_per_split, a.kb_total);
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
+            record_error(a.err, kErrTimeoutSmemEmpty);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], L::W_BYTES + L::X_BYTES);
+          tma_load_2d(sW + stage * L::W_BYTES, &tmW, &full[stage], kb * BK, nt * BW, pw);
+          tma_load_2d(sX + stage * L::X_BYTES, &tmX, &full[stage], kb * BK, mt * BT, px);
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BW, BT);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      for (int u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x, ++it) {
+        int mt, nt, s;
+        decode_unit(u, mt, nt, s);
+        const int kb0 = s * a.kb_per_split;
+        const int kb1 = min(kb0 + a.kb_per_split, a.kb_total);
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag)) {
+          record_error(a.err, kErrTimeoutTmemEmpty);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BT);
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            record_error(a.err, kErrTimeoutTmaFull);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t wb = smem_u32(sW + stage * L::W_BYTES);
+          const uint32_t xb = smem_u32(sX + stage * L::X_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / UK; ++k) {
+            tc_mma_f16(d_tmem, sw128_kmajor_desc(wb + k * UK * 2),
+                       sw128_kmajor_desc(xb + k * UK * 2), idesc,
+                       (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&tfull[acc]);
+      }
+    }
+  } else {
+    // ---------------- epilogue warps ----------------
+    const int quad = warp & 3;           // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + lane;    // weight row within the tile == TMEM lane
+    const int etid = threadIdx.x - 64;   // 0..127
+    int it = 0;
+    for (int u = blockIdx.x; u < total; u += gridDim.x, ++it) {
+      int mt, nt, s;
+      decode_unit(u, mt, nt, s);
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      // One thread waits (bounded); the decision is broadcast so that all 128 epilogue
+      // threads take the same path through the named barriers below.
+      if (etid == 0) {
+        int go = 1;
+        if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
+          record_error(a.err, kErrTimeoutTmemFull);
+          *abort_flag = 1;
+          go = 0;
+        }
+        s_go[it & 1] = go;
+      }
+      named_bar_sync(1, 128);
+      if (!s_go[it & 1]) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                             static_cast<uint32_t>(acc * BT);
+      const int tile = mt * a.n_tiles + nt;
+      const int m0 = mt * BT;
+      const int n = nt * BW + row;
+
+      auto emit = [&](const float* v, int c) {
+        // v[0..CH) are columns (tokens) m0+c .. m0+c+CH-1 of weight row `row`.
+        if (a.mode == kEpiSwiGLU) {
+          if (row >= 64) {
+#pragma unroll
+            for (int j = 0; j < CH; ++j) sEpi[(row - 64) * (CH + 1) + j] = v[j];
+          }
+          named_bar_sync(1, 128);
+          if (row < 64) {
+            const int f = nt * 64 + row;
+            const int nf = a.N >> 1;
+            bf16* C = reinterpret_cast<bf16*>(a.C);
+            if (f < nf) {
+#pragma unroll
+              for (int j = 0; j < CH; ++j) {
+                const int m = m0 + c + j;
+                if (m < a.M) {
+                  const float g = v[j];
+                  const float up = sEpi[row * (CH + 1) + j];
+                  C[static_cast<size_t>(m) * a.ldc + f] = __float2bfloat16(silu(g) * up);
+                }
+              }
+            }
+          }
+          named_bar_sync(1, 128);
+        } else if (n < a.N) {
+          if (a.mode == kEpiF32) {
+            float* C = reinterpret_cast<float*>(a.C);
+#pragma unroll
+            for (int j = 0; j < CH; ++j) {
+              const int m = m0 + c + j;
+              if (m < a.M) C[static_cast<size_t>(m) * a.ldc + n] = v[j];
+            }
+          } else {
+            bf16* C = reinterpret_cast<bf16*>(a.C);
+#pragma unroll
+            for (int j = 0; j < CH; ++j) {
+              const int m = m0 + c + j;
+              if (m < a.M) {
+                float x = v[j];
+                if (a.residual != nullptr)
+                  x += __bfloat162float(a.residual[static_cast<size_t>(m) * a.ldr + n]);
+                C[static_cast<size_t>(m) * a.ldc + n] = __float2bfloat16(x);
+              }
+            }
+          }
+        }
+      };
+
+      float v[CH];
+      if (a.splits == 1) {
+#pragma unroll 1
+        for (int c = 0; c < BT; c += CH) {
+          uint32_t r[CH];
+          if constexpr (CH == 32) {
+            tmem_ld32(tbase + c, *reinterpret_cast<uint32_t(*)[32]>(r));
+          } else {
+            tmem_ld16(tbase + c, *reinterpret_cast<uint32_t(*)[16]>(r));
+          }
+          tc_wait_ld();
+          if (c + CH >= BT) {
+            tc_fence_before();
+            mbar_arrive(&tempty[acc]);
+          }
+#pragma unroll
+          for (int j = 0; j < CH; ++j) v[j] = __uint_as_float(r[j]);
+          emit(v, c);
+        }
+      } else {
+        // split-K: stash fp32 partial, last arriving CTA reduces in split order.
+        float* wsp = a.ws + (static_cast<size_t>(tile) * a.splits + s) * BT * BW;
+#pragma unroll 1
+        for (int c = 0; c < BT; c += CH) {
+          uint32_t r[CH];
+          if constexpr (CH == 32) {
+            tmem_ld32(tbase + c, *reinterpret_cast<uint32_t(*)[32]>(r));
+          } else {
+            tmem_ld16(tbase + c, *reinterpret_cast<uint32_t(*)[16]>(r));
+          }
+          tc_wait_ld();
+          if (c + CH >= BT) {
+            tc_fence_before();
+            mbar_arrive(&tempty[acc]);
+          }
+#pragma unroll
+          for (int j = 0; j < CH; ++j) __stcg(&wsp[(c + j) * BW + row], __uint_as_float(r[j]));
+        }
+        __threadfence();
+        named_bar_sync(1, 128);
+        if (etid == 0) {
+          const int prev = atomicAdd(&a.counters[tile], 1);
+          *s_last = (prev == a.splits - 1) ? 1 : 0;
+        }
+        named_bar_sync(1, 128);
+        if (*s_last) {
+          __threadfence();
+          const float* base = a.ws + static_cast<size_t>(tile) * a.splits * BT * BW;
+#pragma unroll 1
+          for (int c = 0; c < BT; c += CH) {
+#pragma unroll
+            for (int j = 0; j < CH; ++j) v[j] = 0.f;
+            for (int sp = 0; sp < a.splits; ++sp) {
+              const float* p = base + static_cast<size_t>(sp) * BT * BW;
+#pragma unroll
+              for (int j = 0; j < CH; ++j) v[j] += __ldcg(&p[(c + j) * BW + row]);
+            }
+            emit(v, c);
+          }
+          if (etid == 0) a.counters[tile] = 0;
+        }
+      }
+    }
+  }
+
+  __syncthreads();
+  if (*abort_flag) {
+    // Unwind: wait (bounded) for our own TMA loads and MMAs still in flight.
+    if (warp == 0 && lane == 0) {
+      for (int s = 0; s < STAGES; ++s)
+        if (issued_mask & (1u << s))
+          if (!mbar_wait(&full[s], (issued_parity >> s) & 1u, nullptr, kWaitBudgetNs))
+            record_error(a.err, kErrTimeoutDrain);
+    }
+    if (warp == 1 && lane == 0) {
+      tc_commit(drain);
+      if (!mbar_wait(drain, 0, nullptr, kWaitBudgetNs)) record_error(a.err, kErrTimeoutDrain);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::TMEM_COLS);
+  }
+}
+
+// ======================================================================================
+// Host side
+// ======================================================================================
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    TORCH_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && p != nullptr,
+                "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map (inner = contiguous dim) with 128-byte swizzle and a 64 x box_rows box.
+CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t inner, uint64_t outer,
+                              uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                              CUtensorMapSwizzle swz) {
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(ptr) % 16 == 0, "TMA base must be 16-byte aligned");
+  TORCH_CHECK(row_stride_bytes % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims,
+                           strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", static_cast<int>(r));
+  return m;
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int BT, int STAGES>
+static void launch_bt(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a, int grid,
+                      cudaStream_t st) {
+  using L = GemmSmem<BT, STAGES>;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(gemm_tc_kernel<BT, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         L::TOTAL);
+    attr = true;
+  }
+  gemm_tc_kernel<BT, STAGES><<<grid, kThreads, L::TOTAL, st>>>(tw, tx, a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+static int pick_bt(int M) {
+  if (M <= 16) return 16;
+  if (M <= 32) return 32;
+  if (M <= 64) return 64;
+  if (M <= 128) return 128;
+  return 256;
+}
+
+// Choose the split-K factor that best fills the SMs (fewest idle SM-slots in the last wave).
+static int pick_splits(int tiles, int kb_total, int sms) {
+  if (tiles >= sms || kb_total < 4) return 1;
+  int best = 1;
+  double best_eff = 0;
+  const int max_s = std::min(16, kb_total / 2);
+  for (int s = 1; s <= max_s; ++s) {
+    const int units = tiles * s;
+    const int waves = (units + sms - 1) / sms;
+    const double eff = static_cast<double>(units) / (static_cast<double>(waves) * sms);
+    if (eff > best_eff + 0.02) {
+      best_eff = eff;
+      best = s;
+    }
+  }
+  return best;
+}
+
+// Returns the (bt, splits) plan so Python can size workspaces.
+std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t bt, int64_t splits) {
+  const int BT = bt > 0 ? static_cast<int>(bt) : pick_bt(static_cast<int>(M));
+  const int m_tiles = (M + BT - 1) / BT;
+  const int n_tiles = (N + BW - 1) / BW;
+  const int kb_total = (K + BK - 1) / BK;
+  int sp = splits > 0 ? static_cast<int>(splits) : pick_splits(m_tiles * n_tiles, kb_total, num_sms());
+  sp = std::max(1, std::min(sp, kb_total));
+  const int kbps = (kb_total + sp - 1) / sp;
+  sp = (kb_total + kbps - 1) / kbps;  // no empty splits
+  const int64_t ws_floats = sp > 1 ? static_cast<int64_t>(m_tiles) * n_tiles * sp * BT * BW : 0;
+  return {BT, sp, m_tiles * n_tiles, ws_floats};
+}
+
+void gemm_bf16(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
+               const c10::optional<at::Tensor>& residual, int64_t mode, at::Tensor& ws,
+               at::Tensor& counters, at::Tensor& err, int64_t bt, int64_t splits) {
+  TORCH_CHECK(A.is_cuda() && W.is_cuda() && C.is_cuda(), "gemm: tensors must be CUDA");
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && W.scalar_type() == at::kBFloat16,
+              "gemm: A and W must be bf16");
+  TORCH_CHECK(A.dim() == 2 && W.dim() == 2 && C.dim() == 2, "gemm: 2-D tensors expected");
+  TORCH_CHECK(A.stride(1) == 1 && W.stride(1) == 1 && C.stride(1) == 1, "gemm: inner stride 1");
+  const int M = A.size(0), K = A.size(1), N = W.size(0);
+  TORCH_CHECK(W.size(1) == K, "gemm: K mismatch");
+  TORCH_CHECK(K % 8 == 0, "gemm: K must be a multiple of 8 (16-byte TMA rows)");
+  if (M == 0) return;
+  if (mode == kEpiSwiGLU) {
+    TORCH_CHECK(N % 128 == 0, "swiglu gemm: N must be a multiple of 128");
+    TORCH_CHECK(C.size(1) >= N / 2 && C.size(0) >= M, "swiglu gemm: C too small");
+    TORCH_CHECK(C.scalar_type() == at::kBFloat16, "swiglu gemm: bf16 out");
+  } else if (mode == kEpiF32) {
+    TORCH_CHECK(C.scalar_type() == at::kFloat && C.size(1) >= N && C.size(0) >= M, "f32 out");
+  } else {
+    TORCH_CHECK(C.scalar_type() == at::kBFloat16 && C.size(1) >= N && C.size(0) >= M, "bf16 out");
+  }
+  auto plan = gemm_plan(M, N, K, bt, splits);
+  const int BT = plan[0];
+  int sp = plan[1];
+  const int tiles = plan[2];
+  if (sp > 1) {
+    if (ws.numel() < plan[3] || counters.numel() < tiles) {
+      sp = 1;  // workspace too small for this plan: fall back to no split
+    }
+  }
+  const int kb_total = (K + BK - 1) / BK;
+  const int kbps = (kb_total + sp - 1) / sp;
+
+  GemmArgs a;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.m_tiles = (M + BT - 1) / BT;
+  a.n_tiles = (N + BW - 1) / BW;
+  a.splits = sp;
+  a.kb_per_split = kbps;
+  a.kb_total = kb_total;
+  a.C = C.data_ptr();
+  a.ldc = C.stride(0);
+  a.residual = nullptr;
+  a.ldr = 0;
+  if (residual.has_value() && residual->defined()) {
+    TORCH_CHECK(mode == kEpiStore, "residual only with bf16 store");
+    TORCH_CHECK(residual->scalar_type() == at::kBFloat16 && residual->stride(1) == 1, "residual");
+    a.residual = reinterpret_cast<const bf16*>(residual->data_ptr());
+    a.ldr = residual->stride(0);
+  }
+  a.ws = sp > 1 ? ws.data_ptr<float>() : nullptr;
+  a.counters = sp > 1 ? counters.data_ptr<int>() : nullptr;
+  a.mode = mode;
+  a.err = err.data_ptr<int>();
+
+  const CUtensorMap tw = make_tmap_bf16_2d(W.data_ptr(), K, N, W.stride(0) * 2, BK, BW,
+                                           CU_TENSOR_MAP_SWIZZLE_128B);
+  const CUtensorMap tx = make_tmap_bf16_2d(A.data_ptr(), K, M, A.stride(0) * 2, BK, BT,
+                                           CU_TENSOR_MAP_SWIZZLE_128B);
+  const int units = a.m_tiles * a.n_tiles * sp;
+  const int grid = std::min(units, num_sms());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  switch (BT) {
+    case 16: launch_bt<16, 8>(tw, tx, a, grid, st); break;
+    case 32: launch_bt<32, 8>(tw, tx, a, grid, st); break;
+    case 64: launch_bt<64, 8>(tw, tx, a, grid, st); break;
+    case 128: launch_bt<128, 6>(tw, tx, a, grid, st); break;
+    case 256: launch_bt<256, 4>(tw, tx, a, grid, st); break;
+    default: TORCH_CHECK(false, "gemm: unsupported token tile ", BT);
+  }
+}
+
+}  // namespace lb

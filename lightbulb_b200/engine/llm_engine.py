@@ -1,0 +1,238 @@
+"""LLMEngine: the public offline/serving API.
+
+Replaces the reference's ``ModelRunner`` thread + ``EngineModel`` trait
+(``src/engine/model_runner.rs:129-528``) and the model managers
+(``src/model/parallel_model_manager.rs``, ``src/model_fuel/engine_model.rs``) with a
+continuous-batching engine:
+
+    eng = LLMEngine.from_pretrained(path)            # safetensors dir / .gguf / AWQ dir
+    eng.add_request("r1", prompt="...", params=SamplingParams(max_tokens=64))
+    while eng.has_unfinished(): outs = eng.step()    # one scheduler iteration
+    eng.generate(["a", "b"], params)                 # convenience
+
+Every ``step()`` copies that step's inputs host->device from pinned memory and reads the
+sampled ids back device->host (``last_step_io``).
+"""
+from __future__ import annotations
+
+import logging
+import os
+import time
+import uuid
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Sequence as Seq, Union
+
+import torch
+
+from ..config import CacheConfig, EngineConfig, ModelConfig, SchedulerConfig
+from ..kv.block_manager import BlockManager
+from ..models.llama import KVCache, LlamaModel
+from .model_runner import ModelRunner
+from .sampling import SamplingParams
+from .scheduler import Scheduler
+from .sequence import Sequence, SeqStatus, effective_generation_budget
+from .tokenizer import BaseTokenizer, ByteTokenizer, IncrementalDetokenizer
+
+log = logging.getLogger("lightbulb_b200.engine")
+
+
+@dataclass
+class RequestOutput:
+    request_id: str
+    new_token_ids: List[int]
+    new_text: str
+    finished: bool
+    finish_reason: Optional[str] = None
+    prompt_tokens: int = 0
+    completion_tokens: int = 0
+    cached_tokens: int = 0
+
+
+@dataclass
+class EngineStats:
+    steps: int = 0
+    prompt_tokens: int = 0
+    generated_tokens: int = 0
+    preemptions: int = 0
+    ttfts: List[float] = field(default_factory=list)
+    itls: List[float] = field(default_factory=list)
+    finished: int = 0
+
+
+def derive_num_blocks(cfg: ModelConfig, cache: CacheConfig, tp_size: int, device,
+                      reserve_bytes: int = 6 << 30) -> int:
+    if cache.num_blocks > 0:
+        return cache.num_blocks
+    hkv = max(1, cfg.num_kv_heads // tp_size)
+    per_block = KVCache.bytes_per_block(cfg.num_layers, hkv, cache.block_size, cfg.head_dim)
+    if torch.device(device).type != "cuda":
+        return max(64, (512 << 20) // per_block)
+    free, _total = torch.cuda.mem_get_info(torch.device(device))
+    avail = int(free * cache.gpu_memory_utilization) - reserve_bytes
+    return max(16, avail // per_block)
+
+
+class LLMEngine:
+    def __init__(self, cfg: EngineConfig, packed_weights: dict,
+                 tokenizer: Optional[BaseTokenizer] = None, comm=None, tp_rank: int = 0,
+                 tp_size: int = 1, model: Optional[LlamaModel] = None):
+        self.cfg = cfg
+        mcfg = cfg.model
+        dev = packed_weights["embed"].device
+        self.device = dev
+        self.tokenizer = tokenizer or ByteTokenizer(mcfg.vocab_size)
+        self.eos_ids = set(mcfg.eos_ids())
+        if self.tokenizer.eos_token_ids:
+            self.eos_ids |= set(self.tokenizer.eos_token_ids)
+        max_len = cfg.scheduler.max_model_len
+        self.model = model or LlamaModel(mcfg, packed_weights, tp_rank, tp_size,
+                                         max_positions=max_len + 64, comm=comm)
+        nb = derive_num_blocks(mcfg, cfg.cache, tp_size, dev)
+        if comm is not None and comm.world > 1:
+            nb = comm.min_int(nb)  # every rank must admit identically
+        self.kv = KVCache(mcfg.num_layers, nb, self.model.hkv, cfg.cache.block_size,
+                          mcfg.head_dim, device=dev)
+        self.blocks = BlockManager(nb, cfg.cache.block_size, cfg.cache.enable_prefix_caching)
+        self.scheduler = Scheduler(cfg.scheduler, self.blocks)
+        self.runner = ModelRunner(self.model, self.kv, self.blocks, cfg.scheduler.max_num_seqs,
+                                  cfg.scheduler.max_num_batched_tokens, max_len,
+                                  use_cuda_graphs=cfg.use_cuda_graphs, comm=comm)
+        self.seqs: Dict[str, Sequence] = {}
+        self.detok: Dict[str, IncrementalDetokenizer] = {}
+        self.stats = EngineStats()
+        self.spec = None  # speculative decoder (engine/speculative.py) when configured
+        self.kv_policy = None  # KV compression policy (kv/compression.py) when configured
+        log.info("engine ready: %d KV blocks of %d tokens (%.1f GiB)", nb, cfg.cache.block_size,
+                 self.kv.storage.numel() * 2 / 2**30)
+
+    # ---------------------------------------------------------------------------------
+    @classmethod
+    def from_pretrained(cls, path: str, engine_cfg: Optional[EngineConfig] = None,
+                        device: str = "cuda", **kw) -> "LLMEngine":
+        from ..models.loader import load_model_dir
+        mcfg, packed, tok = load_model_dir(path, device=device)
+        cfg = engine_cfg or EngineConfig()
+        cfg.model = mcfg
+        return cls(cfg, packed, tok, **kw)
+
+    @classmethod
+    def random_init(cls, mcfg: ModelConfig, engine_cfg: Optional[EngineConfig] = None,
+                    device: str = "cuda", seed: int = 0, **kw) -> "LLMEngine":
+        from ..models.weights import random_packed_model
+        cfg = engine_cfg or EngineConfig()
+        cfg.model = mcfg
+        packed = random_packed_model(mcfg, seed=seed, device=device)
+        return cls(cfg, packed, None, **kw)
+
+    # ---------------------------------------------------------------------------------
+    def add_request(self, request_id: Optional[str] = None, prompt: Optional[str] = None,
+                    params: Optional[SamplingParams] = None,
+                    prompt_token_ids: Optional[List[int]] = None, priority: int = 1,
+                    add_special_tokens: bool = True) -> Sequence:
+        rid = request_id or uuid.uuid4().hex
+        params = params or SamplingParams()
+        if prompt_token_ids is None:
+            prompt_token_ids = self.tokenizer.encode(prompt or "", add_special_tokens)
+        if not prompt_token_ids:
+            prompt_token_ids = [self.tokenizer.bos_token_id or 0]
+        max_len = self.cfg.scheduler.max_model_len
+        if len(prompt_token_ids) >= max_len:
+            prompt_token_ids = prompt_token_ids[-(max_len - 1):]
+        budget, trunc = effective_generation_budget(len(prompt_token_ids), params.max_tokens,
+                                                    max_len)
+        seq = Sequence(rid, list(prompt_token_ids), params, priority=priority)
+        seq.max_new_tokens = budget
+        seq.truncated = trunc
+        if rid in self.seqs and not self.seqs[rid].finished:
+            raise ValueError(f"duplicate request id {rid}")
+        self.seqs[rid] = seq
+        self.detok[rid] = IncrementalDetokenizer(self.tokenizer)
+        self.scheduler.add(seq)
+        self.stats.prompt_tokens += len(prompt_token_ids)
+        return seq
+
+    def abort(self, request_id: str) -> None:
+        self.scheduler.abort(request_id)
+
+    def has_unfinished(self) -> bool:
+        return self.scheduler.has_work()
+
+    # ---------------------------------------------------------------------------------
+    def step(self) -> List[RequestOutput]:
+        if self.spec is not None and self.spec.active:
+            return self.spec.step(self)
+        so = self.scheduler.schedule()
+        if so.empty:
+            return []
+        res = self.runner.execute(so)
+        return self._process(res.chunks, res.tokens)
+
+    def _process(self, chunks, tokens) -> List[RequestOutput]:
+        now = time.perf_counter()
+        outs: List[RequestOutput] = []
+        ti = 0
+        self.stats.steps += 1
+        for c in chunks:
+            seq = c.seq
+            seq.num_computed_tokens += c.num_tokens
+            if not c.needs_logits:
+                continue
+            tok = tokens[ti]
+            ti += 1
+            if seq.finished:
+                continue
+            outs.append(self._append_token(seq, tok, now))
+        if self.kv_policy is not None:
+            self.kv_policy.after_step(self)
+        return outs
+
+    def _append_token(self, seq: Sequence, tok: int, now: float) -> RequestOutput:
+        seq.output_token_ids.append(tok)
+        if seq.first_token_time is None:
+            seq.first_token_time = now
+            self.stats.ttfts.append(now - seq.arrival_time)
+        elif seq.token_times:
+            self.stats.itls.append(now - seq.token_times[-1])
+        seq.token_times.append(now)
+        self.stats.generated_tokens += 1
+        delta = self.detok[seq.request_id].push(tok)
+        seq.output_text += delta
+        reason = None
+        p = seq.params
+        if not p.ignore_eos and (tok in self.eos_ids or tok in p.stop_token_ids):
+            reason = "stop"
+        elif p.stop and any(s in seq.output_text for s in p.stop):
+            reason = "stop"
+            for s in p.stop:
+                k = seq.output_text.find(s)
+                if k >= 0:
+                    seq.output_text = seq.output_text[:k]
+        elif len(seq.output_token_ids) >= seq.max_new_tokens:
+            reason = "length"
+        elif seq.num_tokens >= self.cfg.scheduler.max_model_len:
+            reason = "length"
+        if reason is not None:
+            self.scheduler.finish(seq, reason)
+            self.stats.finished += 1
+        return RequestOutput(seq.request_id, [tok], delta, reason is not None, reason,
+                             seq.prompt_len, len(seq.output_token_ids), seq.num_cached_prefix)
+
+    # ---------------------------------------------------------------------------------
+    def generate(self, prompts: Union[str, List[str], None] = None,
+                 params: Optional[SamplingParams] = None,
+                 prompt_token_ids: Optional[List[List[int]]] = None) -> List[Sequence]:
+        if isinstance(prompts, str):
+            prompts = [prompts]
+        seqs = []
+        if prompt_token_ids is not None:
+            for ids in prompt_token_ids:
+                seqs.append(self.add_request(params=params, prompt_token_ids=ids))
+        else:
+            for p in prompts or []:
+                seqs.append(self.add_request(prompt=p, params=params))
+        while any(not s.finished for s in seqs):
+            self.step()
+        return seqs
+
+    def last_step_io(self):
+        return self.runner.h2d_bytes, self.runner.d2h_bytes

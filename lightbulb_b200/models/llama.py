@@ -1,0 +1,148 @@
+"""Llama-family decoder over the sm_100a op set, with a paged KV cache.
+
+Covers the reference's model graph (``src/model/custom_transformer.rs:450-628``
+BatchedTransformer, ``custom_transformer_block.rs:304-357`` pre-LN blocks,
+``custom_attention.rs:250-674`` attention, ``mlp_wrapper.rs:154-199`` SwiGLU) and the Fuel
+batched paged decoder (``src/model_fuel/batched.rs:570-826``) in one forward that mixes
+decode rows and chunked-prefill rows in the same step:
+
+* one fused QKV GEMM, RoPE + paged KV append in one kernel (per-row positions);
+* paged attention: the decode kernel for single-token rows, the prefill kernel for the rest;
+* o_proj -> fused residual add + RMSNorm -> gate_up GEMM with SwiGLU epilogue -> down_proj ->
+  fused residual add + next layer's RMSNorm;
+* logits (fp32) only for the rows that sample.
+
+Tensor parallelism (``comm`` hooks) is injected by :mod:`lightbulb_b200.parallel.tp`.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable, List, Optional
+
+import torch
+
+from .. import ops
+from ..config import ModelConfig
+
+
+class KVCache:
+    """Paged KV storage: per layer K and V tensors of shape [num_blocks, Hkv, BS, D]."""
+
+    def __init__(self, num_layers: int, num_blocks: int, num_kv_heads: int, block_size: int,
+                 head_dim: int, dtype=torch.bfloat16, device="cuda"):
+        self.num_layers = num_layers
+        self.num_blocks = num_blocks
+        self.block_size = block_size
+        self.num_kv_heads = num_kv_heads
+        self.head_dim = head_dim
+        self.storage = torch.zeros(num_layers, 2, num_blocks, num_kv_heads, block_size, head_dim,
+                                   dtype=dtype, device=device)
+        self.k = [self.storage[i, 0] for i in range(num_layers)]
+        self.v = [self.storage[i, 1] for i in range(num_layers)]
+
+    @staticmethod
+    def bytes_per_block(num_layers, num_kv_heads, block_size, head_dim, elt=2) -> int:
+        return num_layers * 2 * num_kv_heads * block_size * head_dim * elt
+
+    def copy_blocks(self, pairs: List[int]) -> None:
+        """Copy-on-write: pairs = [src0, dst0, src1, dst1, ...]."""
+        if not pairs:
+            return
+        src = torch.tensor(pairs[0::2], device=self.storage.device, dtype=torch.long)
+        dst = torch.tensor(pairs[1::2], device=self.storage.device, dtype=torch.long)
+        self.storage[:, :, dst] = self.storage[:, :, src]
+
+
+@dataclass
+class ForwardBatch:
+    """Device-side inputs of one forward step (tokens ordered: decode seqs first)."""
+
+    input_ids: torch.Tensor      # [T] int32
+    positions: torch.Tensor      # [T] int32
+    slots: torch.Tensor          # [T] int32 (block * BS + offset, -1 = no KV write)
+    block_tables: torch.Tensor   # [B, W] int32
+    seq_lens: torch.Tensor       # [B] int32: KV length after this step
+    cu_q: torch.Tensor           # [B + 1] int32
+    logits_idx: torch.Tensor     # [R] int64 rows that produce logits
+    num_decode: int              # first num_decode sequences have exactly one query token
+    tile_seq: Optional[torch.Tensor] = None    # prefill attention work list
+    tile_row0: Optional[torch.Tensor] = None
+    decode_splits: int = 1
+    seq_lens_cpu: Optional[torch.Tensor] = None
+    cu_q_cpu: Optional[torch.Tensor] = None
+
+    @property
+    def num_tokens(self) -> int:
+        return self.input_ids.shape[0]
+
+
+def prefill_tiles(cu_q: List[int], first_seq: int, group: int, rows_per_tile: int = 64):
+    """Work list for the prefill attention kernel: (seq, first packed row) per CTA."""
+    seqs, rows = [], []
+    for s in range(first_seq, len(cu_q) - 1):
+        n = (cu_q[s + 1] - cu_q[s]) * group
+        for r in range(0, n, rows_per_tile):
+            seqs.append(s)
+            rows.append(r)
+    return seqs, rows
+
+
+class LlamaModel:
+    """Weights in device layout (see ``models/weights.py``) + forward."""
+
+    def __init__(self, cfg: ModelConfig, packed: dict, tp_rank: int = 0, tp_size: int = 1,
+                 max_positions: Optional[int] = None, comm=None):
+        self.cfg = cfg
+        self.w = packed
+        self.layers = packed["layers"]
+        self.tp_rank, self.tp_size = tp_rank, tp_size
+        self.hq = cfg.num_heads // tp_size
+        self.hkv = max(1, cfg.num_kv_heads // tp_size)
+        self.d = cfg.head_dim
+        self.group = self.hq // self.hkv
+        self.device = packed["embed"].device
+        mp = max_positions or cfg.max_position_embeddings
+        self.cos_sin = ops.rope_table(mp, cfg.head_dim, cfg.rope_theta, self.device)
+        self.comm = comm  # tensor-parallel communicator (None = single GPU)
+        self.vocab_local = packed["lm_head"].shape[0]
+
+    # ------------------------------------------------------------------------------
+    def forward(self, b: ForwardBatch, kv: KVCache) -> torch.Tensor:
+        """Returns fp32 logits [len(b.logits_idx), vocab_local]."""
+        cfg = self.cfg
+        T = b.num_tokens
+        hq, hkv, d = self.hq, self.hkv, self.d
+        eps = cfg.rms_norm_eps
+        dev = self.device
+        comm = self.comm
+
+        x = ops.embedding(b.input_ids, self.w["embed"])          # residual stream [T, H]
+        h = ops.rmsnorm(x, self.layers[0]["ln_in"], eps)
+        attn = torch.empty(T, hq * d, dtype=torch.bfloat16, device=dev)
+        nd = b.num_decode
+        for i, L in enumerate(self.layers):
+            qkv = ops.gemm(h, L["qkv"])
+            ops.rope_kv(qkv, b.positions, b.slots, self.cos_sin, kv.k[i], kv.v[i], hq, hkv)
+            q = qkv[:, :hq * d].view(T, hq, d)
+            a3 = attn.view(T, hq, d)
+            if nd > 0:
+                ops.paged_attention(q, kv.k[i], kv.v[i], b.block_tables, b.seq_lens, b.cu_q,
+                                    a3, self.group, decode=True, num_splits=b.decode_splits,
+                                    seq_lens_cpu=b.seq_lens_cpu, cu_q_cpu=b.cu_q_cpu)
+            if b.tile_seq is not None and b.tile_seq.numel() > 0:
+                ops.paged_attention(q, kv.k[i], kv.v[i], b.block_tables, b.seq_lens, b.cu_q,
+                                    a3, self.group, decode=False, tile_seq=b.tile_seq,
+                                    tile_row0=b.tile_row0, seq_lens_cpu=b.seq_lens_cpu,
+                                    cu_q_cpu=b.cu_q_cpu)
+            o = ops.gemm(attn, L["o"])
+            if comm is not None:
+                o = comm.all_reduce(o)
+            h = ops.rmsnorm(o, L["ln_post"], eps, residual=x)
+            act = ops.gemm(h, L["gate_up"], mode=ops.EPI_SWIGLU)
+            dn = ops.gemm(act, L["down"])
+            if comm is not None:
+                dn = comm.all_reduce(dn)
+            nw = self.layers[i + 1]["ln_in"] if i + 1 < len(self.layers) else self.w["norm"]
+            h = ops.rmsnorm(dn, nw, eps, residual=x)
+        hl = h.index_select(0, b.logits_idx) if b.logits_idx.numel() != T else h
+        return ops.gemm(hl, self.w["lm_head"], mode=ops.EPI_F32)

@@ -1,0 +1,293 @@
+"""Operator layer.
+
+CUDA tensors are served by the hand-written sm_100a kernels in ``lightbulb_b200._C``; if
+that extension is missing on a CUDA device every op raises (there is no silent eager
+fallback on the GPU).  CPU tensors are served by plain-PyTorch restatements of the same
+math so that the engine, scheduler and model plumbing run in CPU tests.
+"""
+from __future__ import annotations
+
+import math
+import threading
+from typing import Optional
+
+import torch
+
+try:  # the extension is built in-tree by ``python setup.py build_ext --inplace``
+    from .. import _C  # type: ignore
+except Exception as _e:  # pragma: no cover - exercised on machines without the build
+    _C = None
+    _C_ERR = _e
+else:
+    _C_ERR = None
+
+EPI_STORE, EPI_SWIGLU, EPI_F32 = 0, 1, 2
+
+# Number of our own CUDA kernels launched (eager calls counted here; CUDA-graph replays add
+# the count recorded when the graph was captured).
+_launches = [0]
+
+
+def launch_counter_reset() -> None:
+    _launches[0] = 0
+
+
+def launch_counter_value() -> int:
+    return _launches[0]
+
+
+def launch_counter_add(n: int) -> None:
+    _launches[0] += n
+
+
+def have_cuda_kernels() -> bool:
+    return _C is not None
+
+
+def _need_c():
+    if _C is None:
+        raise RuntimeError(
+            "lightbulb_b200._C (sm_100a kernels) is not built; run `python setup.py build_ext "
+            f"--inplace`: {_C_ERR}")
+    return _C
+
+
+class _DeviceScratch:
+    """Per-device workspaces shared by kernels that run back to back on one stream:
+    split-K partial tiles + tile counters for the GEMM, split-KV partials for attention,
+    and the device error word every bounded wait reports into."""
+
+    def __init__(self, device: torch.device, ws_floats: int = 24 << 20):
+        self.device = device
+        self.gemm_ws = torch.empty(ws_floats, dtype=torch.float32, device=device)
+        self.gemm_counters = torch.zeros(1 << 16, dtype=torch.int32, device=device)
+        self.err = torch.zeros(4, dtype=torch.int32, device=device)
+        self.attn_o: Optional[torch.Tensor] = None
+        self.attn_lse: Optional[torch.Tensor] = None
+        self._retired: list = []
+
+    def attn_buffers(self, splits: int, rows: int, d: int):
+        need = splits * rows
+        if self.attn_lse is None or self.attn_lse.numel() < need:
+            # Never free a replaced buffer: captured CUDA graphs may still point at it.
+            if self.attn_o is not None:
+                self._retired.append((self.attn_o, self.attn_lse))
+            need = max(need, 1 << 16)
+            self.attn_o = torch.empty(need * d, dtype=torch.float32, device=self.device)
+            self.attn_lse = torch.empty(need, dtype=torch.float32, device=self.device)
+        return self.attn_o, self.attn_lse
+
+
+_scratch: dict = {}
+_lock = threading.Lock()
+
+
+def scratch(device: torch.device) -> _DeviceScratch:
+    key = (device.type, device.index if device.index is not None else torch.cuda.current_device())
+    s = _scratch.get(key)
+    if s is None:
+        with _lock:
+            s = _scratch.get(key)
+            if s is None:
+                s = _DeviceScratch(torch.device("cuda", key[1]))
+                _scratch[key] = s
+    return s
+
+
+class KernelError(RuntimeError):
+    pass
+
+
+_ERR_NAMES = {1: "TMA load wait timed out", 2: "smem slot wait timed out",
+              3: "TMEM accumulator wait timed out", 4: "TMEM release wait timed out",
+              5: "peer flag wait timed out", 6: "index out of bounds", 7: "drain timed out"}
+
+
+def check_errors(device: Optional[torch.device] = None, reset: bool = True) -> None:
+    """Raise if any kernel on ``device`` recorded an error (bounded wait expired, OOB)."""
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    s = scratch(dev)
+    code = int(s.err[0].item())
+    if code:
+        if reset:
+            s.err.zero_()
+        raise KernelError(f"device kernel error {code}: {_ERR_NAMES.get(code, '?')}")
+
+
+# ------------------------------------------------------------------------------------
+# GEMM
+# ------------------------------------------------------------------------------------
+def gemm(a: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
+         residual: Optional[torch.Tensor] = None, mode: int = EPI_STORE, bt: int = 0,
+         splits: int = 0) -> torch.Tensor:
+    """``out = a @ w.T`` (+ residual) with epilogue ``mode``:
+    EPI_STORE -> bf16 [M, N]; EPI_F32 -> fp32 [M, N]; EPI_SWIGLU -> bf16 [M, N/2] of
+    ``silu(gate) * up`` for gate/up rows interleaved in 64-row groups."""
+    m, n = a.shape[0], w.shape[0]
+    if out is None:
+        if mode == EPI_SWIGLU:
+            out = torch.empty(m, n // 2, dtype=torch.bfloat16, device=a.device)
+        elif mode == EPI_F32:
+            out = torch.empty(m, n, dtype=torch.float32, device=a.device)
+        else:
+            out = torch.empty(m, n, dtype=torch.bfloat16, device=a.device)
+    if a.is_cuda:
+        C = _need_c()
+        s = scratch(a.device)
+        C.gemm_bf16(a, w, out, residual, mode, s.gemm_ws, s.gemm_counters, s.err, bt, splits)
+        _launches[0] += 1
+        return out
+    # CPU restatement
+    y = a.float() @ w.float().T
+    if mode == EPI_SWIGLU:
+        g = y.view(m, -1, 2, 64)
+        y = (torch.nn.functional.silu(g[:, :, 0]) * g[:, :, 1]).reshape(m, -1)
+        out.copy_(y.to(out.dtype))
+    elif mode == EPI_F32:
+        out.copy_(y)
+    else:
+        if residual is not None:
+            y = y + residual.float()
+        out.copy_(y.to(out.dtype))
+    return out
+
+
+def gemm_plan(m: int, n: int, k: int, bt: int = 0, splits: int = 0):
+    return tuple(_need_c().gemm_plan(m, n, k, bt, splits))
+
+
+# ------------------------------------------------------------------------------------
+# Norm / embedding / rope
+# ------------------------------------------------------------------------------------
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, residual: Optional[torch.Tensor] = None,
+            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """If ``residual`` is given: ``residual += x`` then ``out = rmsnorm(residual)``."""
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    if x.is_cuda:
+        _need_c().rmsnorm(x, residual, w, out, eps)
+        _launches[0] += 1
+        return out
+    if residual is not None:
+        residual.copy_((residual.float() + x.float()).to(residual.dtype))
+        src = residual.float()
+    else:
+        src = x.float()
+    y = src * torch.rsqrt(src.pow(2).mean(-1, keepdim=True) + eps) * w.float()
+    out.copy_(y.to(out.dtype))
+    return out
+
+
+def embedding(ids: torch.Tensor, table: torch.Tensor, out: Optional[torch.Tensor] = None):
+    if out is None:
+        out = torch.empty(ids.shape[0], table.shape[1], dtype=table.dtype, device=table.device)
+    if table.is_cuda:
+        _need_c().embedding(ids, table, out, scratch(table.device).err)
+        _launches[0] += 1
+        return out
+    out.copy_(table[ids.long()])
+    return out
+
+
+def rope_table(max_pos: int, head_dim: int, theta: float, device) -> torch.Tensor:
+    """[max_pos, head_dim] fp32: cos(pos * inv_freq) | sin(pos * inv_freq), computed in fp64."""
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
+    ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None, :]
+    return torch.cat([torch.cos(ang), torch.sin(ang)], dim=1).float().to(device)
+
+
+def rope_kv(qkv: torch.Tensor, positions: torch.Tensor, slots: Optional[torch.Tensor],
+            cos_sin: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, hq: int,
+            hkv: int) -> None:
+    """Rotate q (in place) and k of ``qkv`` [T, (hq + 2 hkv) D] and write k, v to their slots."""
+    if qkv.is_cuda:
+        _need_c().rope_kv(qkv, positions, slots, cos_sin, k_cache, v_cache, hq, hkv,
+                          scratch(qkv.device).err)
+        _launches[0] += 1
+        return
+    d = cos_sin.shape[1]
+    t = qkv.shape[0]
+    half = d // 2
+    cs = cos_sin[positions.long()]
+    c, s = cs[:, None, :half], cs[:, None, half:]
+    x = qkv[:, :(hq + hkv) * d].view(t, hq + hkv, d).float()
+    x1, x2 = x[..., :half], x[..., half:]
+    rot = torch.cat([x1 * c - x2 * s, x1 * s + x2 * c], -1).to(qkv.dtype)
+    qkv[:, :hq * d].copy_(rot[:, :hq].reshape(t, -1))
+    if slots is not None:
+        bs = k_cache.shape[2]
+        sl = slots.long()
+        ok = sl >= 0
+        blk, off = sl[ok] // bs, sl[ok] % bs
+        k = rot[:, hq:][ok]
+        v = qkv[:, (hq + hkv) * d:(hq + 2 * hkv) * d].view(t, hkv, d)[ok]
+        k_cache[blk, :, off] = k
+        v_cache[blk, :, off] = v
+
+
+# ------------------------------------------------------------------------------------
+# Attention
+# ------------------------------------------------------------------------------------
+def decode_splits(num_seqs: int, num_kv_heads: int, max_kv_len: int, sms: int = 148) -> int:
+    """Split-KV factor for decode: enough CTAs to cover the SMs twice, each split >= 256 keys."""
+    ctas = num_seqs * num_kv_heads
+    if ctas >= 2 * sms:
+        return 1
+    s = max(1, min((2 * sms + ctas - 1) // ctas, max(1, max_kv_len // 256), 32))
+    return s
+
+
+def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                    block_tables: torch.Tensor, seq_lens: torch.Tensor, cu_q: torch.Tensor,
+                    out: torch.Tensor, group: int, decode: bool,
+                    tile_seq: Optional[torch.Tensor] = None,
+                    tile_row0: Optional[torch.Tensor] = None, num_splits: int = 1,
+                    causal: bool = True, seq_lens_cpu=None, cu_q_cpu=None) -> torch.Tensor:
+    """q: [T, Hq, D] (may be a strided view of the QKV buffer); out: [T, Hq, D]."""
+    d = q.shape[-1]
+    scale = 1.0 / math.sqrt(d)
+    if q.is_cuda:
+        C = _need_c()
+        po = pl = None
+        if decode and num_splits > 1:
+            po, pl = scratch(q.device).attn_buffers(num_splits, q.shape[0] * q.shape[1], d)
+        C.paged_attention(q, k_cache, v_cache, out, block_tables, seq_lens, cu_q, tile_seq,
+                          tile_row0, group, scale, decode, num_splits, po, pl, causal)
+        _launches[0] += 2 if (decode and num_splits > 1) else 1
+        return out
+    # CPU restatement
+    bs = k_cache.shape[2]
+    sl = (seq_lens_cpu if seq_lens_cpu is not None else seq_lens).tolist()
+    cq = (cu_q_cpu if cu_q_cpu is not None else cu_q).tolist()
+    from ..models.reference import attention_ref
+    for i, L in enumerate(sl):
+        q0, q1 = cq[i], cq[i + 1]
+        if q1 == q0:
+            continue
+        nb = (L + bs - 1) // bs
+        blocks = block_tables[i, :nb].long()
+        k = k_cache[blocks].permute(0, 2, 1, 3).reshape(nb * bs, k_cache.shape[1], d)[:L]
+        v = v_cache[blocks].permute(0, 2, 1, 3).reshape(nb * bs, v_cache.shape[1], d)[:L]
+        qpos = torch.arange(L - (q1 - q0), L)
+        o = attention_ref(q[q0:q1], k, v, qpos, torch.arange(L), causal=causal)
+        out[q0:q1] = o.to(out.dtype)
+    return out
+
+
+# ------------------------------------------------------------------------------------
+# Sampling
+# ------------------------------------------------------------------------------------
+def sample(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor,
+           top_p: torch.Tensor, seeds: torch.Tensor, out: Optional[torch.Tensor] = None,
+           logprobs: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+    if logits.is_cuda:
+        _need_c().sample_tokens(logits, temperature, top_k, top_p, seeds, out, logprobs)
+        _launches[0] += 1
+        return out
+    from ..engine.sampling import sample_row_reference
+    for r in range(logits.shape[0]):
+        out[r] = sample_row_reference(logits[r], float(temperature[r]), int(top_k[r]),
+                                      float(top_p[r]), int(seeds[r]))
+    return out

@@ -1,0 +1,89 @@
+"""Tensor-parallel communicator (one process per GPU, NCCL over NVLink / NVSwitch).
+
+Replaces the reference's in-process "collectives" (``src/multi_gpu/tensor_parallel.rs:119-188``:
+``to_device`` + add on device 0, ``CommunicationBackend::NCCL`` dead code at
+``src/multi_gpu/config.rs:163-170``) with real collectives:
+
+* ``all_reduce`` of the row-parallel partial outputs (o_proj, down_proj);
+* vocab-parallel sampling: greedy rows reduce (max, first index) across ranks; sampled rows
+  all-gather the logits of those rows and run the sampling kernel on every rank with the
+  same seed, so every rank sees the same token without a broadcast;
+* ``min_int`` so that all ranks size the KV pool identically and schedule identically.
+
+This NCCL path is the baseline arm.  The fused GEMM + collective kernels over peer memory
+(:mod:`lightbulb_b200.parallel.fused`) replace ``all_reduce`` on the hot path.
+"""
+from __future__ import annotations
+
+import os
+from datetime import timedelta
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+
+
+def init_distributed(backend: Optional[str] = None, timeout_s: float = 120.0):
+    """Initialise the default process group from torchrun's environment.  Returns
+    (rank, world, local_rank)."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        be = backend or ("nccl" if torch.cuda.is_available() else "gloo")
+        if be == "nccl":
+            torch.cuda.set_device(local)
+        kw = {"device_id": torch.device("cuda", local)} if be == "nccl" else {}
+        dist.init_process_group(be, timeout=timedelta(seconds=timeout_s), **kw)
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return rank, world, local
+
+
+class TPComm:
+    def __init__(self, group=None):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.fused = None  # set by parallel.fused when peer-memory kernels are enabled
+
+    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        if self.world > 1:
+            dist.all_reduce(x, group=self.group)
+        return x
+
+    def min_int(self, v: int) -> int:
+        if self.world == 1:
+            return v
+        dev = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() \
+            else torch.device("cpu")
+        t = torch.tensor([v], dtype=torch.int64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN, group=self.group)
+        return int(t.item())
+
+    def max_float(self, v: float) -> float:
+        if self.world == 1:
+            return v
+        dev = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() \
+            else torch.device("cpu")
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+        return float(t.item())
+
+    def barrier(self):
+        if self.world > 1:
+            dist.barrier(group=self.group)
+
+    def sample_vocab_parallel(self, logits: torch.Tensor, temp: torch.Tensor,
+                              top_k: torch.Tensor, top_p: torch.Tensor, seeds: torch.Tensor,
+                              out_tokens: torch.Tensor) -> None:
+        """logits: [B, V/world] fp32 shard of this rank.  Writes identical tokens on every
+        rank.  Always all-gathers the shards (one collective, graph-capturable), then runs
+        the device sampling kernel on the full rows."""
+        b, vl = logits.shape
+        full = torch.empty(self.world, b, vl, dtype=logits.dtype, device=logits.device)
+        dist.all_gather_into_tensor(full, logits.contiguous(), group=self.group)
+        full = full.permute(1, 0, 2).reshape(b, self.world * vl)
+        ops.sample(full, temp, top_k, top_p, seeds, out_tokens)

@@ -1,0 +1,218 @@
+"""Numerics of the sm_100a kernels against plain PyTorch fp32 references."""
+import math
+
+import pytest
+import torch
+
+from lightbulb_b200 import ops
+from lightbulb_b200.models.reference import attention_ref
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / (b.float().norm() + 1e-12)).item()
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 128, 64), (7, 384, 512), (16, 256, 4096), (33, 1000, 256),
+                                   (100, 640, 1024), (256, 768, 4096), (300, 512, 2048),
+                                   (1000, 1024, 512), (2048, 2048, 1024)])
+def test_gemm_store(m, n, k):
+    torch.manual_seed(m * 7 + n)
+    a = torch.randn(m, k, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(n, k, device=DEV) * 0.05).to(torch.bfloat16)
+    ref = a.float() @ w.float().T
+    out = ops.gemm(a, w)
+    torch.cuda.synchronize()
+    ops.check_errors()
+    assert _rel(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 5])
+@pytest.mark.parametrize("bt", [16, 64, 256])
+def test_gemm_splitk_tiles(splits, bt):
+    torch.manual_seed(splits + bt)
+    m, n, k = 77, 512, 2048
+    a = torch.randn(m, k, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(n, k, device=DEV) * 0.05).to(torch.bfloat16)
+    ref = a.float() @ w.float().T
+    for _ in range(2):  # second call reuses the zeroed counters
+        out = ops.gemm(a, w, bt=bt, splits=splits)
+        torch.cuda.synchronize()
+        assert _rel(out, ref) < 1e-2
+    ops.check_errors()
+
+
+def test_gemm_residual_and_f32():
+    m, n, k = 50, 384, 1024
+    a = torch.randn(m, k, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(n, k, device=DEV) * 0.05).to(torch.bfloat16)
+    r = torch.randn(m, n, device=DEV).to(torch.bfloat16)
+    ref = a.float() @ w.float().T
+    out = ops.gemm(a, w, residual=r)
+    assert _rel(out, ref + r.float()) < 1e-2
+    o32 = ops.gemm(a, w, mode=ops.EPI_F32)
+    assert o32.dtype == torch.float32 and _rel(o32, ref) < 5e-3
+
+
+@pytest.mark.parametrize("m", [3, 64, 200])
+def test_gemm_swiglu(m):
+    from lightbulb_b200.models.weights import interleave_gate_up
+    f, k = 384, 512
+    a = torch.randn(m, k, device=DEV).to(torch.bfloat16)
+    g = (torch.randn(f, k, device=DEV) * 0.05).to(torch.bfloat16)
+    u = (torch.randn(f, k, device=DEV) * 0.05).to(torch.bfloat16)
+    w = interleave_gate_up(g, u)
+    ref = torch.nn.functional.silu(a.float() @ g.float().T) * (a.float() @ u.float().T)
+    for sp in (1, 3):
+        out = ops.gemm(a, w, mode=ops.EPI_SWIGLU, splits=sp)
+        assert out.shape == (m, f)
+        assert _rel(out, ref) < 1e-2
+
+
+def test_rmsnorm_and_fused_add():
+    x = torch.randn(37, 4096, device=DEV).to(torch.bfloat16)
+    r = torch.randn(37, 4096, device=DEV).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(4096, device=DEV)).to(torch.bfloat16)
+    y = ops.rmsnorm(x, w, 1e-5)
+    xf = x.float()
+    ref = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5) * w.float()
+    assert _rel(y, ref) < 1e-2
+    r2 = r.clone()
+    y2 = ops.rmsnorm(x, w, 1e-5, residual=r2)
+    s = (r.float() + x.float()).to(torch.bfloat16).float()
+    assert torch.equal(r2.float(), s)
+    ref2 = s * torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + 1e-5) * w.float()
+    assert _rel(y2, ref2) < 1e-2
+
+
+def test_embedding():
+    tab = torch.randn(1000, 256, device=DEV).to(torch.bfloat16)
+    ids = torch.tensor([0, 5, 999, 5], dtype=torch.int32, device=DEV)
+    assert torch.equal(ops.embedding(ids, tab), tab[ids.long()])
+
+
+def test_rope_kv():
+    hq, hkv, d, bs = 8, 2, 128, 16
+    T = 40
+    qkv = torch.randn(T, (hq + 2 * hkv) * d, device=DEV).to(torch.bfloat16)
+    pos = torch.randint(0, 500, (T,), dtype=torch.int32, device=DEV)
+    slots = torch.randperm(64 * bs, device=DEV)[:T].to(torch.int32)
+    slots[3] = -1
+    cs = ops.rope_table(1024, d, 1e4, DEV)
+    kc = torch.zeros(64, hkv, bs, d, device=DEV, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    q_in = qkv.clone()
+    ops.rope_kv(qkv, pos, slots, cs, kc, vc, hq, hkv)
+    # CPU restatement
+    qc = q_in.cpu()
+    kc2 = torch.zeros(64, hkv, bs, d, dtype=torch.bfloat16)
+    vc2 = torch.zeros_like(kc2)
+    ops.rope_kv(qc, pos.cpu(), slots.cpu(), cs.cpu(), kc2, vc2, hq, hkv)
+    assert _rel(qkv[:, :hq * d].cpu(), qc[:, :hq * d]) < 1e-2
+    assert _rel(kc.cpu(), kc2) < 1e-2
+    assert torch.equal(vc.cpu(), vc2)
+
+
+def _paged_setup(seq_lens, q_lens, hq, hkv, d=128, bs=16, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    nb_per = [(L + bs - 1) // bs for L in seq_lens]
+    nblocks = sum(nb_per) + 4
+    perm = torch.randperm(nblocks, generator=g)
+    kc = torch.randn(nblocks, hkv, bs, d, generator=g).to(torch.bfloat16)
+    vc = torch.randn(nblocks, hkv, bs, d, generator=g).to(torch.bfloat16)
+    W = max(nb_per)
+    bt = torch.zeros(len(seq_lens), W, dtype=torch.int32)
+    o = 0
+    for i, n in enumerate(nb_per):
+        bt[i, :n] = perm[o:o + n].to(torch.int32)
+        o += n
+    T = sum(q_lens)
+    q = torch.randn(T, hq, d, generator=g).to(torch.bfloat16)
+    cu = torch.tensor([0] + list(torch.tensor(q_lens).cumsum(0).tolist()), dtype=torch.int32)
+    return q, kc, vc, bt, torch.tensor(seq_lens, dtype=torch.int32), cu
+
+
+def _ref_paged(q, kc, vc, bt, sl, cu, bs=16):
+    outs = []
+    for i in range(len(sl)):
+        L = int(sl[i])
+        q0, q1 = int(cu[i]), int(cu[i + 1])
+        nb = (L + bs - 1) // bs
+        blk = bt[i, :nb].long()
+        k = kc[blk].permute(0, 2, 1, 3).reshape(nb * bs, kc.shape[1], -1)[:L]
+        v = vc[blk].permute(0, 2, 1, 3).reshape(nb * bs, vc.shape[1], -1)[:L]
+        outs.append(attention_ref(q[q0:q1], k, v, torch.arange(L - (q1 - q0), L), torch.arange(L)))
+    return torch.cat(outs, 0)
+
+
+@pytest.mark.parametrize("hq,hkv", [(32, 8), (4, 1), (8, 8), (8, 1)])
+@pytest.mark.parametrize("splits", [1, 4])
+def test_paged_decode(hq, hkv, splits):
+    seq_lens = [1, 15, 16, 17, 100, 1000, 2049]
+    q, kc, vc, bt, sl, cu = _paged_setup(seq_lens, [1] * len(seq_lens), hq, hkv)
+    ref = _ref_paged(q, kc, vc, bt, sl, cu)
+    out = torch.empty(q.shape, dtype=torch.bfloat16, device=DEV)
+    ops.paged_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), sl.to(DEV), cu.to(DEV),
+                        out, hq // hkv, decode=True, num_splits=splits)
+    torch.cuda.synchronize()
+    assert _rel(out.cpu(), ref) < 2e-2
+
+
+@pytest.mark.parametrize("hq,hkv", [(32, 8), (4, 1), (8, 8)])
+def test_paged_prefill_chunked(hq, hkv):
+    from lightbulb_b200.models.llama import prefill_tiles
+    seq_lens = [5, 64, 130, 700, 513]
+    q_lens = [5, 64, 30, 512, 1]      # chunked: queries are the tail of each sequence
+    q, kc, vc, bt, sl, cu = _paged_setup(seq_lens, q_lens, hq, hkv, seed=3)
+    ref = _ref_paged(q, kc, vc, bt, sl, cu)
+    ts, tr = prefill_tiles(cu.tolist(), 0, hq // hkv)
+    out = torch.empty(q.shape, dtype=torch.bfloat16, device=DEV)
+    ops.paged_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), sl.to(DEV), cu.to(DEV),
+                        out, hq // hkv, decode=False,
+                        tile_seq=torch.tensor(ts, dtype=torch.int32, device=DEV),
+                        tile_row0=torch.tensor(tr, dtype=torch.int32, device=DEV))
+    torch.cuda.synchronize()
+    assert _rel(out.cpu(), ref) < 2e-2
+
+
+def test_sampling_greedy_and_topk_topp():
+    from lightbulb_b200.engine.sampling import sample_row_reference
+    torch.manual_seed(0)
+    B, V = 6, 128256
+    logits = torch.randn(B, V, device=DEV) * 3
+    logits[0, 777] = 50.0
+    logits[1, 5] = logits[1, 9] = 40.0  # tie -> first index
+    temp = torch.tensor([0.0, 0.0, 0.7, 1.0, 1.3, 0.9], device=DEV)
+    topk = torch.tensor([0, 0, 50, 0, 1, 20], dtype=torch.int32, device=DEV)
+    topp = torch.tensor([1.0, 1.0, 1.0, 0.9, 1.0, 0.5], device=DEV)
+    seeds = torch.tensor([1, 2, 3, 4, 5, 6], dtype=torch.int64, device=DEV)
+    out = ops.sample(logits, temp, topk, topp, seeds)
+    torch.cuda.synchronize()
+    o = out.tolist()
+    assert o[0] == 777 and o[1] == 5
+    assert o[4] == int(torch.argmax(logits[4]))  # top-k 1 is greedy
+    for r in (2, 3, 5):
+        exp = sample_row_reference(logits[r].cpu(), float(temp[r]), int(topk[r]),
+                                   float(topp[r]), int(seeds[r]))
+        assert o[r] == exp
+    # top-k restricts support
+    kth = torch.topk(logits[2], 50).values[-1]
+    assert logits[2, o[2]] >= kth
+
+
+def test_sampling_distribution():
+    V = 1000
+    logits = torch.zeros(1, V, device=DEV)
+    logits[0, :4] = torch.tensor([2.0, 1.0, 0.5, 0.0])
+    logits[0, 4:] = -30
+    counts = torch.zeros(V)
+    for s in range(400):
+        t = ops.sample(logits, torch.tensor([1.0], device=DEV),
+                       torch.tensor([0], dtype=torch.int32, device=DEV),
+                       torch.tensor([1.0], device=DEV),
+                       torch.tensor([s * 7919 + 1], dtype=torch.int64, device=DEV))
+        counts[int(t)] += 1
+    p = torch.softmax(torch.tensor([2.0, 1.0, 0.5, 0.0]), 0)
+    assert torch.allclose(counts[:4] / 400, p, atol=0.08)
