@@ -45,7 +45,7 @@ class _GraphBucket:
         W = r.max_blocks_per_seq
         self.W = W
         # int32 layout: ids | pos | slots | seq_lens | cu_q(B+1) | top_k | block_tables(B*W)
-        self.n_int = 5 * bsz + 1 + bsz * W
+        self.n_int = 6 * bsz + 1 + bsz * W
         self.ints = torch.zeros(self.n_int, dtype=torch.int32, device=dev)
         self.floats = torch.zeros(2 * bsz, dtype=torch.float32, device=dev)
         self.seeds = torch.zeros(bsz, dtype=torch.int64, device=dev)

@@ -231,7 +231,7 @@ def rope_kv(qkv: torch.Tensor, positions: torch.Tensor, slots: Optional[torch.Te
 def decode_splits(num_seqs: int, num_kv_heads: int, max_kv_len: int, sms: int = 148) -> int:
     """Split-KV factor for decode: enough CTAs to cover the SMs twice, each split >= 256 keys."""
     ctas = num_seqs * num_kv_heads
-    if ctas >= 2 * sms:
+    if ctas == 0 or ctas >= 2 * sms:
         return 1
     s = max(1, min((2 * sms + ctas - 1) // ctas, max(1, max_kv_len // 256), 32))
     return s
