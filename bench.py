@@ -161,7 +161,7 @@ def main():
     for _ in range(args.requests):
         L = rng.randint(args.min_prompt, args.max_prompt)
         prompts.append([rng.randrange(mcfg.vocab_size) for _ in range(L)])
-    sp = SamplingParams(temperature=0.0, max_tokens=out_len, ignore_eos=True)
+    sp = SamplingParams(temperature=0.0, max_tokens=out_len, ignore_eos=True, detokenize=False)
 
     # Capture the decode graph for the full batch before any request arrives.
     if not args.no_graphs:

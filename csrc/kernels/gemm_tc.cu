@@ -375,6 +375,275 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ======================================================================================
+// Cluster split-K variant for small token counts (decode).  The S CTAs of a thread-block
+// cluster own the same 128 x BT output tile and split K; each stages its fp32 partial in
+// its own shared memory (the drained pipeline buffers) and the tile is reduced through
+// distributed shared memory: CTA r sums every peer's partial for the 32-column chunks
+// c with c % S == r, in fixed rank order (deterministic), then runs the epilogue.  No
+// global workspace, no atomics, no multicast.
+// ======================================================================================
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+template <int BT, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_cluster_kernel(const __grid_constant__ CUtensorMap tmW,
+                           const __grid_constant__ CUtensorMap tmX, const GemmArgs a) {
+  using L = GemmSmem<BT, STAGES>;
+  constexpr int CH = L::CH;
+  constexpr int TMEM_COLS = BT < 32 ? 32 : BT;
+  static_assert(BT * BW * 4 <= STAGES * (L::W_BYTES + L::X_BYTES), "partial must fit");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sW = smem;
+  uint8_t* sX = smem + STAGES * L::W_BYTES;
+  float* sPart = reinterpret_cast<float*>(smem);  // reused after the main loop: [BT][128]
+  float* sEpi = reinterpret_cast<float*>(sX + STAGES * L::X_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* drain = tfull + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* s_go = reinterpret_cast<volatile int*>(tmem_slot + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t S = cluster_nctarank();
+  const uint32_t rank = cluster_ctarank();
+  const int tile = blockIdx.x / S;
+  const int mt = tile % a.m_tiles;
+  const int nt = tile / a.m_tiles;
+  const int kb0 = rank * a.kb_per_split;
+  const int kb1 = min(kb0 + a.kb_per_split, a.kb_total);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmW);
+    prefetch_tmap(&tmX);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  uint32_t issued_mask = 0, issued_parity = 0;
+  bool mma_issued = false;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pw = policy_evict_first();
+      const uint64_t px = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
+          record_error(a.err, kErrTimeoutSmemEmpty);
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[stage], L::W_BYTES + L::X_BYTES);
+        tma_load_2d(sW + stage * L::W_BYTES, &tmW, &full[stage], kb * BK, nt * BW, pw);
+        tma_load_2d(sX + stage * L::X_BYTES, &tmX, &full[stage], kb * BK, mt * BT, px);
+        issued_mask |= 1u << stage;
+        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BW, BT);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&full[stage], phase, abort_flag)) {
+          record_error(a.err, kErrTimeoutTmaFull);
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t wb = smem_u32(sW + stage * L::W_BYTES);
+        const uint32_t xb = smem_u32(sX + stage * L::X_BYTES);
+#pragma unroll
+        for (int k = 0; k < BK / UK; ++k)
+          tc_mma_f16(tmem_base, sw128_kmajor_desc(wb + k * UK * 2),
+                     sw128_kmajor_desc(xb + k * UK * 2), idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+        mma_issued = true;
+        tc_commit(&empty[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (ok) tc_commit(tfull);
+    }
+  } else {
+    // Epilogue warps: TMEM -> own shared-memory partial [BT][128] (column-major by token).
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const int etid = threadIdx.x - 64;
+    if (etid == 0) {
+      int go = 1;
+      if (kb1 <= kb0) {
+        go = 2;  // empty split: contributes zeros
+      } else if (!mbar_wait(tfull, 0, abort_flag)) {
+        record_error(a.err, kErrTimeoutTmemFull);
+        *abort_flag = 1;
+        go = 0;
+      }
+      s_go[0] = go;
+    }
+    named_bar_sync(1, 128);
+    const int go = s_go[0];
+    if (go == 1) {
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < BT; c += CH) {
+        uint32_t r[CH];
+        if constexpr (CH == 32) {
+          tmem_ld32(tbase + c, *reinterpret_cast<uint32_t(*)[32]>(r));
+        } else {
+          tmem_ld16(tbase + c, *reinterpret_cast<uint32_t(*)[16]>(r));
+        }
+        tc_wait_ld();
+#pragma unroll
+        for (int j = 0; j < CH; ++j) sPart[(c + j) * BW + row] = __uint_as_float(r[j]);
+      }
+    } else {
+      for (int c = 0; c < BT; ++c) sPart[c * BW + row] = 0.f;
+    }
+  }
+
+  // Every partial of the cluster is in shared memory after this barrier.
+  tc_fence_before();
+  cluster_sync_all();
+
+  if (warp >= 2) {
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const int m0 = mt * BT;
+    const int n = nt * BW + row;
+    const uint32_t my_part = smem_u32(sPart);
+    float v[CH];
+#pragma unroll 1
+    for (int ci = rank; ci < BT / CH; ci += S) {
+      const int c = ci * CH;
+#pragma unroll
+      for (int j = 0; j < CH; ++j) v[j] = 0.f;
+      for (uint32_t sp = 0; sp < S; ++sp) {
+        const uint32_t base = mapa_shared(my_part, sp);
+#pragma unroll
+        for (int j = 0; j < CH; ++j) v[j] += ld_dsmem_f32(base + ((c + j) * BW + row) * 4);
+      }
+      if (a.mode == kEpiSwiGLU) {
+        if (row >= 64) {
+#pragma unroll
+          for (int j = 0; j < CH; ++j) sEpi[(row - 64) * (CH + 1) + j] = v[j];
+        }
+        named_bar_sync(1, 128);
+        if (row < 64) {
+          const int f = nt * 64 + row;
+          bf16* C = reinterpret_cast<bf16*>(a.C);
+          if (f < (a.N >> 1)) {
+#pragma unroll
+            for (int j = 0; j < CH; ++j) {
+              const int m = m0 + c + j;
+              if (m < a.M)
+                C[static_cast<size_t>(m) * a.ldc + f] =
+                    __float2bfloat16(silu(v[j]) * sEpi[row * (CH + 1) + j]);
+            }
+          }
+        }
+        named_bar_sync(1, 128);
+      } else if (n < a.N) {
+        if (a.mode == kEpiF32) {
+          float* C = reinterpret_cast<float*>(a.C);
+#pragma unroll
+          for (int j = 0; j < CH; ++j) {
+            const int m = m0 + c + j;
+            if (m < a.M) C[static_cast<size_t>(m) * a.ldc + n] = v[j];
+          }
+        } else {
+          bf16* C = reinterpret_cast<bf16*>(a.C);
+#pragma unroll
+          for (int j = 0; j < CH; ++j) {
+            const int m = m0 + c + j;
+            if (m < a.M) {
+              float x = v[j];
+              if (a.residual != nullptr)
+                x += __bfloat162float(a.residual[static_cast<size_t>(m) * a.ldr + n]);
+              C[static_cast<size_t>(m) * a.ldc + n] = __float2bfloat16(x);
+            }
+          }
+        }
+      }
+    }
+  }
+
+  // No CTA may leave while a peer still reads its shared memory.
+  cluster_sync_all();
+  if (*abort_flag) {
+    if (warp == 0 && lane == 0) {
+      for (int s = 0; s < STAGES; ++s)
+        if (issued_mask & (1u << s))
+          if (!mbar_wait(&full[s], (issued_parity >> s) & 1u, nullptr, kWaitBudgetNs))
+            record_error(a.err, kErrTimeoutDrain);
+    }
+    if (warp == 1 && lane == 0 && mma_issued) {
+      tc_commit(drain);
+      if (!mbar_wait(drain, 0, nullptr, kWaitBudgetNs)) record_error(a.err, kErrTimeoutDrain);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ======================================================================================
 // Host side
 // ======================================================================================
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -441,36 +710,102 @@ static int pick_bt(int M) {
   return 256;
 }
 
-// Choose the split-K factor that best fills the SMs (fewest idle SM-slots in the last wave).
-static int pick_splits(int tiles, int kb_total, int sms) {
-  if (tiles >= sms || kb_total < 4) return 1;
-  int best = 1;
-  double best_eff = 0;
-  const int max_s = std::min(16, kb_total / 2);
-  for (int s = 1; s <= max_s; ++s) {
-    const int units = tiles * s;
-    const int waves = (units + sms - 1) / sms;
-    const double eff = static_cast<double>(units) / (static_cast<double>(waves) * sms);
-    if (eff > best_eff + 0.02) {
-      best_eff = eff;
-      best = s;
+template <int BT, int STAGES>
+static int max_active_clusters(int S) {
+  using L = GemmSmem<BT, STAGES>;
+  static int cache[9] = {0};
+  if (S < 1 || S > 8) return 0;
+  if (cache[S] == 0) {
+    cudaFuncSetAttribute(gemm_tc_cluster_kernel<BT, STAGES>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(S * 64);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = L::TOTAL;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = S;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_cluster_kernel<BT, STAGES>, &cfg) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      n = num_sms() / S;
     }
+    cache[S] = std::max(1, n);
+  }
+  return cache[S];
+}
+
+static int active_clusters_for(int BT, int S) {
+  switch (BT) {
+    case 16: return max_active_clusters<16, 8>(S);
+    case 32: return max_active_clusters<32, 8>(S);
+    case 64: return max_active_clusters<64, 8>(S);
+    case 128: return max_active_clusters<128, 6>(S);
+    default: return max_active_clusters<256, 4>(S);
+  }
+}
+
+// Cluster split-K factor: the largest S <= 8 whose grid (tiles x S CTAs) is co-resident in
+// one wave, keeping >= 2 k-blocks per CTA.  0 = the tiles alone fill the GPU (no cluster).
+static int pick_cluster(int BT, int tiles, int kb_total) {
+  if (tiles >= num_sms()) return 0;
+  int best = 1;
+  for (int S = 2; S <= 8; ++S) {
+    if (kb_total / S < 2) break;
+    if (tiles <= active_clusters_for(BT, S)) best = S;
   }
   return best;
 }
 
-// Returns the (bt, splits) plan so Python can size workspaces.
+// Returns {token tile, split (>0: workspace split-K, <0: cluster split-K of -S CTAs),
+// tile count, workspace floats} so Python can inspect / size workspaces.
 std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t bt, int64_t splits) {
   const int BT = bt > 0 ? static_cast<int>(bt) : pick_bt(static_cast<int>(M));
   const int m_tiles = (M + BT - 1) / BT;
   const int n_tiles = (N + BW - 1) / BW;
   const int kb_total = (K + BK - 1) / BK;
-  int sp = splits > 0 ? static_cast<int>(splits) : pick_splits(m_tiles * n_tiles, kb_total, num_sms());
+  const int tiles = m_tiles * n_tiles;
+  if (splits < 0 || (splits == 0 && pick_cluster(BT, tiles, kb_total) > 1)) {
+    int S = splits < 0 ? static_cast<int>(-splits) : pick_cluster(BT, tiles, kb_total);
+    S = std::max(1, std::min(S, std::min(8, kb_total)));
+    return {BT, -S, tiles, 0};
+  }
+  int sp = splits > 0 ? static_cast<int>(splits) : 1;
   sp = std::max(1, std::min(sp, kb_total));
   const int kbps = (kb_total + sp - 1) / sp;
   sp = (kb_total + kbps - 1) / kbps;  // no empty splits
-  const int64_t ws_floats = sp > 1 ? static_cast<int64_t>(m_tiles) * n_tiles * sp * BT * BW : 0;
-  return {BT, sp, m_tiles * n_tiles, ws_floats};
+  const int64_t ws_floats = sp > 1 ? static_cast<int64_t>(tiles) * sp * BT * BW : 0;
+  return {BT, sp, tiles, ws_floats};
+}
+
+template <int BT, int STAGES>
+static void launch_cluster(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a,
+                           int S, cudaStream_t st) {
+  using L = GemmSmem<BT, STAGES>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(gemm_tc_cluster_kernel<BT, STAGES>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.m_tiles * a.n_tiles * S);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = L::TOTAL;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = S;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_tc_cluster_kernel<BT, STAGES>, tw, tx, a));
 }
 
 void gemm_bf16(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
@@ -498,13 +833,11 @@ void gemm_bf16(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
   const int BT = plan[0];
   int sp = plan[1];
   const int tiles = plan[2];
-  if (sp > 1) {
-    if (ws.numel() < plan[3] || counters.numel() < tiles) {
-      sp = 1;  // workspace too small for this plan: fall back to no split
-    }
-  }
+  if (sp > 1 && (ws.numel() < plan[3] || counters.numel() < tiles)) sp = 1;
   const int kb_total = (K + BK - 1) / BK;
-  const int kbps = (kb_total + sp - 1) / sp;
+  const int S = sp < 0 ? -sp : 1;
+  const int nsplit = sp < 0 ? S : sp;
+  const int kbps = (kb_total + nsplit - 1) / nsplit;
 
   GemmArgs a;
   a.M = M;
@@ -512,7 +845,7 @@ void gemm_bf16(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
   a.K = K;
   a.m_tiles = (M + BT - 1) / BT;
   a.n_tiles = (N + BW - 1) / BW;
-  a.splits = sp;
+  a.splits = sp > 0 ? sp : 1;
   a.kb_per_split = kbps;
   a.kb_total = kb_total;
   a.C = C.data_ptr();
@@ -534,9 +867,20 @@ void gemm_bf16(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
                                            CU_TENSOR_MAP_SWIZZLE_128B);
   const CUtensorMap tx = make_tmap_bf16_2d(A.data_ptr(), K, M, A.stride(0) * 2, BK, BT,
                                            CU_TENSOR_MAP_SWIZZLE_128B);
-  const int units = a.m_tiles * a.n_tiles * sp;
-  const int grid = std::min(units, num_sms());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (sp < 0) {
+    switch (BT) {
+      case 16: launch_cluster<16, 8>(tw, tx, a, S, st); break;
+      case 32: launch_cluster<32, 8>(tw, tx, a, S, st); break;
+      case 64: launch_cluster<64, 8>(tw, tx, a, S, st); break;
+      case 128: launch_cluster<128, 6>(tw, tx, a, S, st); break;
+      case 256: launch_cluster<256, 4>(tw, tx, a, S, st); break;
+      default: TORCH_CHECK(false, "gemm: unsupported token tile ", BT);
+    }
+    return;
+  }
+  const int units = a.m_tiles * a.n_tiles * a.splits;
+  const int grid = std::min(units, num_sms());
   switch (BT) {
     case 16: launch_bt<16, 8>(tw, tx, a, grid, st); break;
     case 32: launch_bt<32, 8>(tw, tx, a, grid, st); break;

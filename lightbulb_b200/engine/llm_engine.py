@@ -100,6 +100,7 @@ class LLMEngine:
         self.seqs: Dict[str, Sequence] = {}
         self.detok: Dict[str, IncrementalDetokenizer] = {}
         self.stats = EngineStats()
+        self.detokenize = True  # incremental text per token (off for token-id-only clients)
         self.spec = None  # speculative decoder (engine/speculative.py) when configured
         self.kv_policy = None  # KV compression policy (kv/compression.py) when configured
         log.info("engine ready: %d KV blocks of %d tokens (%.1f GiB)", nb, cfg.cache.block_size,
@@ -187,7 +188,7 @@ class LLMEngine:
         return outs
 
     def _append_token(self, seq: Sequence, tok: int, now: float) -> RequestOutput:
-        seq.output_token_ids.append(tok)
+        seq.append_output(tok)
         if seq.first_token_time is None:
             seq.first_token_time = now
             self.stats.ttfts.append(now - seq.arrival_time)
@@ -195,8 +196,11 @@ class LLMEngine:
             self.stats.itls.append(now - seq.token_times[-1])
         seq.token_times.append(now)
         self.stats.generated_tokens += 1
-        delta = self.detok[seq.request_id].push(tok)
-        seq.output_text += delta
+        delta = ""
+        p = seq.params
+        if self.detokenize and (p.detokenize or p.stop):
+            delta = self.detok[seq.request_id].push(tok)
+            seq.output_text += delta
         reason = None
         p = seq.params
         if not p.ignore_eos and (tok in self.eos_ids or tok in p.stop_token_ids):

@@ -162,7 +162,9 @@ class ModelRunner:
             temps.append(p.temperature)
             topk.append(p.top_k)
             topp.append(p.top_p)
-            seeds.append(token_seed(c.seq.request_id, len(c.seq.output_token_ids), p.seed))
+            # greedy rows never read their seed: skip the hash
+            seeds.append(token_seed(c.seq.request_id, len(c.seq.output_token_ids), p.seed)
+                         if p.temperature > 0 else 0)
         return temps, topk, topp, seeds
 
     # -------------------------------------------------------------------------------
@@ -198,7 +200,7 @@ class ModelRunner:
         slots[:] = -1
         for i, c in enumerate(chunks):
             s = c.seq
-            ids[i] = s.all_token_ids[c.start]
+            ids[i] = s.last_token
             pos[i] = c.start
             slots[i] = c.slots[0]
             seq_lens[i] = c.start + 1

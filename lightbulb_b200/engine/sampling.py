@@ -31,6 +31,7 @@ class SamplingParams:
     ignore_eos: bool = False
     seed: Optional[int] = None
     logprobs: bool = False
+    detokenize: bool = True  # False: token-id clients, no incremental text
 
     @property
     def greedy(self) -> bool:

@@ -144,7 +144,7 @@ class Scheduler:
                     break
             if seq not in self.running:
                 continue
-            slots, cow = bm.append_slots(seq.seq_id, 1, [seq.all_token_ids[-1]])
+            slots, cow = bm.append_slots(seq.seq_id, 1, [seq.last_token])
             out.cow_pairs += cow
             out.decode.append(ScheduledChunk(seq, seq.num_computed_tokens, 1, slots, True))
             budget -= 1
@@ -194,7 +194,7 @@ class Scheduler:
             seq.status = SeqStatus.RUNNING
             self.running.append(seq)
             if n == 1 and seq.num_uncomputed == 1:
-                slots, cow = bm.append_slots(seq.seq_id, 1, [seq.all_token_ids[-1]])
+                slots, cow = bm.append_slots(seq.seq_id, 1, [seq.last_token])
                 out.cow_pairs += cow
                 out.prefill.append(ScheduledChunk(seq, seq.num_computed_tokens, 1, slots, True))
             else:

@@ -25,7 +25,7 @@ class SeqStatus(enum.Enum):
     FINISHED = "finished"
 
 
-@dataclass
+@dataclass(eq=False)
 class Sequence:
     request_id: str
     prompt_token_ids: List[int]
@@ -48,13 +48,30 @@ class Sequence:
     # speculative decoding
     spec_draft_tokens: List[int] = field(default_factory=list)
 
+    def __post_init__(self) -> None:
+        # prompt + generated ids in one list, appended in place (never rebuilt per step)
+        self._tokens: List[int] = list(self.prompt_token_ids) + list(self.output_token_ids)
+
+    def append_output(self, tok: int) -> None:
+        self.output_token_ids.append(tok)
+        self._tokens.append(tok)
+
+    def truncate_output(self, n: int) -> None:
+        """Keep the first ``n`` generated tokens (speculative rollback)."""
+        del self.output_token_ids[n:]
+        del self._tokens[len(self.prompt_token_ids) + n:]
+
     @property
     def all_token_ids(self) -> List[int]:
-        return self.prompt_token_ids + self.output_token_ids
+        return self._tokens
+
+    @property
+    def last_token(self) -> int:
+        return self._tokens[-1]
 
     @property
     def num_tokens(self) -> int:
-        return len(self.prompt_token_ids) + len(self.output_token_ids)
+        return len(self._tokens)
 
     @property
     def prompt_len(self) -> int:

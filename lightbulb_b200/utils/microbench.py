@@ -1,0 +1,166 @@
+"""Per-op device microbenchmarks of the decode step (CUDA events, warm-up, L2-sized inputs).
+
+    python -m lightbulb_b200.utils.microbench decode --batch 256 --ctx 1200 [--tp 1]
+    python -m lightbulb_b200.utils.microbench gemm --m 256 --n 4096 --k 4096
+
+Reports time, achieved bytes/s or FLOP/s and the fraction of the measured roofline
+(``MEASURED_PEAKS.json`` when present: copy bandwidth and cuBLAS bf16 throughput).
+Weights are distinct per repetition set and larger than L2 so weight streaming is from HBM.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import sys
+
+import torch
+
+from .. import ops
+
+
+def peaks():
+    p = os.path.join(os.path.dirname(__file__), "..", "..", "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return d["hbm_gbs"] * 1e9, d["bf16_tflops"] * 1e12, "measured"
+    except Exception:
+        return 6.65e12, 1.59e15, "fallback"
+
+
+def time_fn(fn, iters=20, warmup=3):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters * 1e3  # us
+
+
+def bench_gemm(m, n, k, copies=None, mode=ops.EPI_STORE, bt=0, splits=0, iters=20):
+    bw, fl, src = peaks()
+    wbytes = n * k * 2
+    copies = copies or max(1, math.ceil(512e6 / wbytes))  # > L2 worth of distinct weights
+    ws = [torch.randn(n, k, device="cuda").to(torch.bfloat16) * 0.02 for _ in range(copies)]
+    a = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+    it = [0]
+
+    def run():
+        ops.gemm(a, ws[it[0] % copies], mode=mode, bt=bt, splits=splits)
+        it[0] += 1
+
+    us = time_fn(run, iters=iters * copies if copies < 8 else iters)
+    it[0] = 0
+
+    def run_cublas():
+        torch.matmul(a, ws[it[0] % copies].T)
+        it[0] += 1
+
+    us_cublas = time_fn(run_cublas, iters=iters * copies if copies < 8 else iters)
+    flops = 2 * m * n * k
+    byts = wbytes + m * k * 2 + m * n * (4 if mode == ops.EPI_F32 else 2)
+    t_roof = max(flops / fl, byts / bw) * 1e6
+    plan = ops.gemm_plan(m, n, k, bt, splits)
+    return {"op": "gemm", "m": m, "n": n, "k": k, "us": round(us, 2),
+            "tflops": round(flops / us / 1e6, 1), "gbs": round(byts / us / 1e3, 1),
+            "roofline_us": round(t_roof, 2), "frac_of_" + src: round(t_roof / us, 3),
+            "plan_bt_splits": plan[:2], "cublas_us": round(us_cublas, 2)}
+
+
+def bench_decode_attn(batch, ctx, hq, hkv, bs=16, splits=None, iters=20):
+    bw, fl, src = peaks()
+    d = 128
+    nb_per = (ctx + bs - 1) // bs
+    nblocks = batch * nb_per + 8
+    kc = torch.empty(nblocks, hkv, bs, d, device="cuda", dtype=torch.bfloat16).normal_()
+    vc = torch.empty_like(kc).normal_()
+    bt = torch.randperm(nblocks, device="cuda")[:batch * nb_per].view(batch, nb_per).int()
+    sl = torch.full((batch,), ctx, dtype=torch.int32, device="cuda")
+    cu = torch.arange(batch + 1, dtype=torch.int32, device="cuda")
+    q = torch.randn(batch, hq, d, device="cuda").to(torch.bfloat16)
+    out = torch.empty_like(q)
+    sp = splits if splits is not None else ops.decode_splits(batch, hkv, ctx)
+
+    def run():
+        ops.paged_attention(q, kc, vc, bt, sl, cu, out, hq // hkv, decode=True, num_splits=sp)
+
+    us = time_fn(run, iters=iters)
+    byts = batch * ctx * hkv * d * 2 * 2
+    return {"op": "attn_decode", "batch": batch, "ctx": ctx, "hq": hq, "hkv": hkv, "splits": sp,
+            "us": round(us, 2), "gbs": round(byts / us / 1e3, 1),
+            "frac_of_" + src: round(byts / bw * 1e6 / us, 3)}
+
+
+def bench_decode(batch, ctx, tp=1, model="llama3-8b"):
+    from ..config import get_preset
+    cfg = get_preset(model)
+    h, f = cfg.hidden_size, cfg.intermediate_size // tp
+    hq, hkv = cfg.num_heads // tp, max(1, cfg.num_kv_heads // tp)
+    d = cfg.head_dim
+    rows = []
+    rows.append(bench_gemm(batch, (hq + 2 * hkv) * d, h))
+    rows.append(bench_gemm(batch, h, hq * d))
+    rows.append(bench_gemm(batch, 2 * f, h, mode=ops.EPI_SWIGLU))
+    rows.append(bench_gemm(batch, h, f))
+    rows.append(bench_gemm(batch, cfg.vocab_size // tp, h, mode=ops.EPI_F32, iters=5))
+    rows.append(bench_decode_attn(batch, ctx, hq, hkv))
+    x = torch.randn(batch, h, device="cuda").to(torch.bfloat16)
+    r = torch.randn(batch, h, device="cuda").to(torch.bfloat16)
+    w = torch.ones(h, device="cuda", dtype=torch.bfloat16)
+    rows.append({"op": "rmsnorm_add", "us": round(time_fn(lambda: ops.rmsnorm(x, w, 1e-5, residual=r)), 2)})
+    qkv = torch.randn(batch, (hq + 2 * hkv) * d, device="cuda").to(torch.bfloat16)
+    pos = torch.arange(batch, dtype=torch.int32, device="cuda")
+    slots = torch.arange(batch, dtype=torch.int32, device="cuda")
+    cs = ops.rope_table(4096, d, cfg.rope_theta, "cuda")
+    kc = torch.zeros(batch, hkv, 16, d, device="cuda", dtype=torch.bfloat16)
+    rows.append({"op": "rope_kv", "us": round(time_fn(
+        lambda: ops.rope_kv(qkv, pos, slots, cs, kc, kc, hq, hkv)), 2)})
+    logits = torch.randn(batch, cfg.vocab_size, device="cuda")
+    z = torch.zeros(batch, device="cuda")
+    zi = torch.zeros(batch, dtype=torch.int32, device="cuda")
+    seeds = torch.zeros(batch, dtype=torch.int64, device="cuda")
+    rows.append({"op": "sample_greedy", "us": round(time_fn(
+        lambda: ops.sample(logits, z, zi, z + 1, seeds)), 2)})
+    per_layer = sum(r["us"] for r in rows[:4]) + rows[5]["us"] + 2 * rows[6]["us"] + rows[7]["us"]
+    total = cfg.num_layers * per_layer + rows[4]["us"] + rows[8]["us"]
+    rows.append({"op": "estimated_step_us", "us": round(total, 1),
+                 "layers": cfg.num_layers, "per_layer_us": round(per_layer, 1)})
+    return rows
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("what", choices=["decode", "gemm", "attn"])
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--ctx", type=int, default=1200)
+    ap.add_argument("--tp", type=int, default=1)
+    ap.add_argument("--m", type=int, default=256)
+    ap.add_argument("--n", type=int, default=4096)
+    ap.add_argument("--k", type=int, default=4096)
+    ap.add_argument("--bt", type=int, default=0)
+    ap.add_argument("--splits", type=int, default=0)
+    ap.add_argument("--hq", type=int, default=32)
+    ap.add_argument("--hkv", type=int, default=8)
+    ap.add_argument("--model", default="llama3-8b")
+    a = ap.parse_args(argv)
+    torch.cuda.set_device(0)
+    if a.what == "decode":
+        rows = bench_decode(a.batch, a.ctx, a.tp, a.model)
+    elif a.what == "gemm":
+        rows = [bench_gemm(a.m, a.n, a.k, bt=a.bt, splits=a.splits)]
+    else:
+        rows = [bench_decode_attn(a.batch, a.ctx, a.hq, a.hkv,
+                                  splits=a.splits if a.splits else None)]
+    for r in rows:
+        print(json.dumps(r))
+    ops.check_errors()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

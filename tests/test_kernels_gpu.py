@@ -216,3 +216,46 @@ def test_sampling_distribution():
         counts[int(t)] += 1
     p = torch.softmax(torch.tensor([2.0, 1.0, 0.5, 0.0]), 0)
     assert torch.allclose(counts[:4] / 400, p, atol=0.08)
+
+
+@pytest.mark.parametrize("S", [1, 2, 3, 4, 8])
+@pytest.mark.parametrize("m,bt", [(5, 16), (64, 64), (256, 256), (130, 128)])
+def test_gemm_cluster_splitk(S, m, bt):
+    torch.manual_seed(S * 100 + m)
+    n, k = 640, 2048
+    a = torch.randn(m, k, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(n, k, device=DEV) * 0.05).to(torch.bfloat16)
+    r = torch.randn(m, n, device=DEV).to(torch.bfloat16)
+    ref = a.float() @ w.float().T
+    out = ops.gemm(a, w, bt=bt, splits=-S)
+    assert _rel(out, ref) < 1e-2
+    out2 = ops.gemm(a, w, residual=r, bt=bt, splits=-S)
+    assert _rel(out2, ref + r.float()) < 1e-2
+    o32 = ops.gemm(a, w, mode=ops.EPI_F32, bt=bt, splits=-S)
+    assert _rel(o32, ref) < 5e-3
+    torch.cuda.synchronize()
+    ops.check_errors()
+
+
+@pytest.mark.parametrize("S", [2, 4])
+def test_gemm_cluster_swiglu_deterministic(S):
+    from lightbulb_b200.models.weights import interleave_gate_up
+    m, f, k = 200, 512, 1024
+    a = torch.randn(m, k, device=DEV).to(torch.bfloat16)
+    g = (torch.randn(f, k, device=DEV) * 0.05).to(torch.bfloat16)
+    u = (torch.randn(f, k, device=DEV) * 0.05).to(torch.bfloat16)
+    w = interleave_gate_up(g, u)
+    ref = torch.nn.functional.silu(a.float() @ g.float().T) * (a.float() @ u.float().T)
+    o1 = ops.gemm(a, w, mode=ops.EPI_SWIGLU, splits=-S)
+    o2 = ops.gemm(a, w, mode=ops.EPI_SWIGLU, splits=-S)
+    assert _rel(o1, ref) < 1e-2
+    assert torch.equal(o1, o2)  # fixed reduction order
+
+
+def test_gemm_auto_plan_decode_shapes():
+    # decode shapes of Llama-3-8B at M=256: automatic plan must be correct too
+    for n, k in [(6144, 4096), (4096, 4096), (4096, 14336)]:
+        a = torch.randn(256, k, device=DEV).to(torch.bfloat16)
+        w = (torch.randn(n, k, device=DEV) * 0.02).to(torch.bfloat16)
+        assert _rel(ops.gemm(a, w), a.float() @ w.float().T) < 1e-2
+    ops.check_errors()
