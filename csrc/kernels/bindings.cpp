@@ -12,6 +12,11 @@ void paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::T
                      const c10::optional<at::Tensor>& tile_row0, int64_t group, double scale,
                      bool decode, int64_t num_splits, const c10::optional<at::Tensor>& part_o,
                      const c10::optional<at::Tensor>& part_lse, bool causal);
+void paged_decode_tma(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                      at::Tensor& out, const at::Tensor& block_tables, const at::Tensor& seq_lens,
+                      int64_t group, double scale, int64_t num_splits,
+                      const c10::optional<at::Tensor>& part_o,
+                      const c10::optional<at::Tensor>& part_lse, at::Tensor& err);
 void embedding(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, at::Tensor& err);
 void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w,
              at::Tensor& y, double eps);
@@ -28,6 +33,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_bf16", &lb::gemm_bf16, "tcgen05 GEMM C = A W^T with fused epilogue");
   m.def("gemm_plan", &lb::gemm_plan, "token tile, split-K and workspace size of a GEMM");
   m.def("paged_attention", &lb::paged_attention, "paged attention (decode / prefill)");
+  m.def("paged_decode_tma", &lb::paged_decode_tma, "TMA-fed warp-specialised paged decode");
   m.def("embedding", &lb::embedding, "embedding gather");
   m.def("rmsnorm", &lb::rmsnorm, "RMSNorm with optional fused residual add");
   m.def("rope_kv", &lb::rope_kv, "RoPE + paged KV append");

@@ -126,8 +126,9 @@ class LlamaModel:
             q = qkv[:, :hq * d].view(T, hq, d)
             a3 = attn.view(T, hq, d)
             if nd > 0:
-                ops.paged_attention(q, kv.k[i], kv.v[i], b.block_tables, b.seq_lens, b.cu_q,
-                                    a3, self.group, decode=True, num_splits=b.decode_splits,
+                ops.paged_attention(q, kv.k[i], kv.v[i], b.block_tables[:nd], b.seq_lens[:nd],
+                                    b.cu_q[:nd + 1], a3, self.group, decode=True,
+                                    num_splits=b.decode_splits,
                                     seq_lens_cpu=b.seq_lens_cpu, cu_q_cpu=b.cu_q_cpu)
             if b.tile_seq is not None and b.tile_seq.numel() > 0:
                 ops.paged_attention(q, kv.k[i], kv.v[i], b.block_tables, b.seq_lens, b.cu_q,

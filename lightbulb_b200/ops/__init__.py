@@ -23,6 +23,11 @@ else:
 
 EPI_STORE, EPI_SWIGLU, EPI_F32 = 0, 1, 2
 
+# Decode attention implementation: "tma" (warp-specialised TMA pipeline, default) or
+# "cpasync" (the generic paged kernel, also used for non-16 block sizes).
+import os as _os
+_DECODE_IMPL = _os.environ.get("LB_DECODE_ATTN", "tma")
+
 # Number of our own CUDA kernels launched (eager calls counted here; CUDA-graph replays add
 # the count recorded when the graph was captured).
 _launches = [0]
@@ -228,13 +233,23 @@ def rope_kv(qkv: torch.Tensor, positions: torch.Tensor, slots: Optional[torch.Te
 # ------------------------------------------------------------------------------------
 # Attention
 # ------------------------------------------------------------------------------------
-def decode_splits(num_seqs: int, num_kv_heads: int, max_kv_len: int, sms: int = 148) -> int:
-    """Split-KV factor for decode: enough CTAs to cover the SMs twice, each split >= 256 keys."""
+def decode_splits(num_seqs: int, num_kv_heads: int, max_kv_len: int, sms: int = 148,
+                  ctas_per_sm: int = 2) -> int:
+    """Split-KV factor for decode: the split count (each split >= 256 keys, <= 32 splits)
+    whose CTA count wastes the least of its last wave of ``sms * ctas_per_sm`` slots."""
     ctas = num_seqs * num_kv_heads
-    if ctas == 0 or ctas >= 2 * sms:
+    slots = sms * ctas_per_sm
+    if ctas == 0 or ctas >= 4 * slots:
         return 1
-    s = max(1, min((2 * sms + ctas - 1) // ctas, max(1, max_kv_len // 256), 32))
-    return s
+    max_s = max(1, min(32, max_kv_len // 256))
+    best, best_eff = 1, 0.0
+    for s in range(1, max_s + 1):
+        n = ctas * s
+        waves = (n + slots - 1) // slots
+        eff = n / (waves * slots)
+        if eff > best_eff + 0.03:
+            best, best_eff = s, eff
+    return best
 
 
 def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
@@ -251,14 +266,21 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
         po = pl = None
         if decode and num_splits > 1:
             po, pl = scratch(q.device).attn_buffers(num_splits, q.shape[0] * q.shape[1], d)
+        if decode and k_cache.shape[2] == 16 and group <= 16 and _DECODE_IMPL == "tma":
+            # one query token per sequence, token i belongs to sequence i
+            C.paged_decode_tma(q, k_cache, v_cache, out, block_tables, seq_lens, group, scale,
+                               num_splits, po, pl, scratch(q.device).err)
+            _launches[0] += 2 if num_splits > 1 else 1
+            return out
         C.paged_attention(q, k_cache, v_cache, out, block_tables, seq_lens, cu_q, tile_seq,
                           tile_row0, group, scale, decode, num_splits, po, pl, causal)
         _launches[0] += 2 if (decode and num_splits > 1) else 1
         return out
     # CPU restatement
     bs = k_cache.shape[2]
-    sl = (seq_lens_cpu if seq_lens_cpu is not None else seq_lens).tolist()
-    cq = (cu_q_cpu if cu_q_cpu is not None else cu_q).tolist()
+    nseq = seq_lens.shape[0]
+    sl = (seq_lens_cpu if seq_lens_cpu is not None else seq_lens).tolist()[:nseq]
+    cq = (cu_q_cpu if cu_q_cpu is not None else cu_q).tolist()[:nseq + 1]
     from ..models.reference import attention_ref
     for i, L in enumerate(sl):
         q0, q1 = cq[i], cq[i + 1]

@@ -259,3 +259,24 @@ def test_gemm_auto_plan_decode_shapes():
         w = (torch.randn(n, k, device=DEV) * 0.02).to(torch.bfloat16)
         assert _rel(ops.gemm(a, w), a.float() @ w.float().T) < 1e-2
     ops.check_errors()
+
+
+@pytest.mark.parametrize("hq,hkv", [(32, 8), (4, 1), (8, 1), (32, 32)])
+@pytest.mark.parametrize("splits", [1, 3])
+def test_paged_decode_tma_vs_cpasync(hq, hkv, splits):
+    import lightbulb_b200.ops as o
+    seq_lens = [1, 15, 16, 17, 63, 64, 65, 100, 1000, 2049]
+    q, kc, vc, bt, sl, cu = _paged_setup(seq_lens, [1] * len(seq_lens), hq, hkv, seed=7)
+    ref = _ref_paged(q, kc, vc, bt, sl, cu)
+    outs = {}
+    for impl in ("tma", "cpasync"):
+        o._DECODE_IMPL = impl
+        out = torch.empty(q.shape, dtype=torch.bfloat16, device=DEV)
+        ops.paged_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), sl.to(DEV),
+                            cu.to(DEV), out, hq // hkv, decode=True, num_splits=splits)
+        torch.cuda.synchronize()
+        outs[impl] = out.cpu()
+    o._DECODE_IMPL = "tma"
+    ops.check_errors()
+    assert _rel(outs["tma"], ref) < 2e-2
+    assert _rel(outs["cpasync"], ref) < 2e-2
