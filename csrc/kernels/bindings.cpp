@@ -4,7 +4,8 @@
 namespace lb {
 void gemm_bf16(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
                const c10::optional<at::Tensor>& residual, int64_t mode, at::Tensor& ws,
-               at::Tensor& counters, at::Tensor& err, int64_t bt, int64_t splits);
+               at::Tensor& counters, at::Tensor& err, int64_t bt, int64_t splits,
+               const c10::optional<at::Tensor>& trace);
 std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t bt, int64_t splits);
 void paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                      at::Tensor& out, const at::Tensor& block_tables, const at::Tensor& seq_lens,
@@ -30,7 +31,10 @@ void sample_tokens(const at::Tensor& logits, const at::Tensor& temperature,
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "lightbulb_b200 sm_100a kernels";
-  m.def("gemm_bf16", &lb::gemm_bf16, "tcgen05 GEMM C = A W^T with fused epilogue");
+  m.def("gemm_bf16", &lb::gemm_bf16, "tcgen05 GEMM C = A W^T with fused epilogue",
+        py::arg("A"), py::arg("W"), py::arg("C"), py::arg("residual"), py::arg("mode"),
+        py::arg("ws"), py::arg("counters"), py::arg("err"), py::arg("bt"), py::arg("splits"),
+        py::arg("trace") = py::none());
   m.def("gemm_plan", &lb::gemm_plan, "token tile, split-K and workspace size of a GEMM");
   m.def("paged_attention", &lb::paged_attention, "paged attention (decode / prefill)");
   m.def("paged_decode_tma", &lb::paged_decode_tma, "TMA-fed warp-specialised paged decode");

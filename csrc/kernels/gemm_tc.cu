@@ -49,6 +49,8 @@ struct GemmArgs {
   int* counters;
   int mode;
   int* err;
+  unsigned long long* trace;  // optional: 8 globaltimer stamps per CTA (phase profiling)
+  int vec_ok;                 // C base 16-byte aligned and ldc % 4 == 0: vector stores
 };
 
 template <int BT, int STAGES>
@@ -400,9 +402,12 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
   return r;
 }
-__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+__device__ __forceinline__ float4 ld_dsmem_f32x4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
   return v;
 }
 
@@ -413,7 +418,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   using L = GemmSmem<BT, STAGES>;
   constexpr int CH = L::CH;
   constexpr int TMEM_COLS = BT < 32 ? 32 : BT;
-  static_assert(BT * BW * 4 <= STAGES * (L::W_BYTES + L::X_BYTES), "partial must fit");
+  // Partial tile staged column-major ([token][weight row]); a CH-column chunk is one
+  // contiguous run of CH*128 floats that the owner CTA reduces as a flat array.
+  static_assert(BW * BT * 4 <= STAGES * (L::W_BYTES + L::X_BYTES), "partial must fit");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -439,6 +446,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nt = tile / a.m_tiles;
   const int kb0 = rank * a.kb_per_split;
   const int kb1 = min(kb0 + a.kb_per_split, a.kb_total);
+  unsigned long long* tr = a.trace ? a.trace + blockIdx.x * 8 : nullptr;
+  if (tr && threadIdx.x == 0) tr[0] = globaltimer_ns();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -464,6 +473,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   uint32_t issued_mask = 0, issued_parity = 0;
   bool mma_issued = false;
+  if (tr && threadIdx.x == 0) tr[1] = globaltimer_ns();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -532,6 +542,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         go = 0;
       }
       s_go[0] = go;
+      if (tr) tr[2] = globaltimer_ns();
     }
     named_bar_sync(1, 128);
     const int go = s_go[0];
@@ -557,63 +568,85 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // Every partial of the cluster is in shared memory after this barrier.
   tc_fence_before();
+  if (tr && threadIdx.x == 64) tr[3] = globaltimer_ns();
   cluster_sync_all();
+  if (tr && threadIdx.x == 64) tr[4] = globaltimer_ns();
 
   if (warp >= 2) {
-    const int quad = warp & 3;
-    const int row = quad * 32 + lane;
+    // Owner of chunk ci (ci % S == rank) reduces it as a flat [CH cols][128 rows] array:
+    // thread e reads float4 number e + 128 q (q < CH/4) from every peer, i.e. token column
+    // j = 4 q + (e >> 5) and weight rows 4 (e & 31) .. +3 -> coalesced 512-byte DSMEM
+    // loads per warp and 4 consecutive output features per lane.
+    constexpr int NQ = CH / 4;
+    const int e = threadIdx.x - 64;
+    const int ew = e >> 5, el = e & 31;
     const int m0 = mt * BT;
-    const int n = nt * BW + row;
     const uint32_t my_part = smem_u32(sPart);
-    float v[CH];
 #pragma unroll 1
     for (int ci = rank; ci < BT / CH; ci += S) {
       const int c = ci * CH;
+      float4 acc[NQ];
 #pragma unroll
-      for (int j = 0; j < CH; ++j) v[j] = 0.f;
-      for (uint32_t sp = 0; sp < S; ++sp) {
-        const uint32_t base = mapa_shared(my_part, sp);
+      for (int q = 0; q < NQ; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+      const uint32_t coff = (c * BW + e * 4) * 4;
+      for (uint32_t sp = 0; sp < S; ++sp) {  // fixed rank order: deterministic
+        const uint32_t b = mapa_shared(my_part, sp) + coff;
+        float4 x[NQ];
 #pragma unroll
-        for (int j = 0; j < CH; ++j) v[j] += ld_dsmem_f32(base + ((c + j) * BW + row) * 4);
+        for (int q = 0; q < NQ; ++q) x[q] = ld_dsmem_f32x4(b + q * 128 * 16);
+#pragma unroll
+        for (int q = 0; q < NQ; ++q) {
+          acc[q].x += x[q].x;
+          acc[q].y += x[q].y;
+          acc[q].z += x[q].z;
+          acc[q].w += x[q].w;
+        }
       }
-      if (a.mode == kEpiSwiGLU) {
-        if (row >= 64) {
 #pragma unroll
-          for (int j = 0; j < CH; ++j) sEpi[(row - 64) * (CH + 1) + j] = v[j];
-        }
-        named_bar_sync(1, 128);
-        if (row < 64) {
-          const int f = nt * 64 + row;
-          bf16* C = reinterpret_cast<bf16*>(a.C);
-          if (f < (a.N >> 1)) {
-#pragma unroll
-            for (int j = 0; j < CH; ++j) {
-              const int m = m0 + c + j;
-              if (m < a.M)
-                C[static_cast<size_t>(m) * a.ldc + f] =
-                    __float2bfloat16(silu(v[j]) * sEpi[row * (CH + 1) + j]);
-            }
-          }
-        }
-        named_bar_sync(1, 128);
-      } else if (n < a.N) {
-        if (a.mode == kEpiF32) {
-          float* C = reinterpret_cast<float*>(a.C);
-#pragma unroll
-          for (int j = 0; j < CH; ++j) {
-            const int m = m0 + c + j;
-            if (m < a.M) C[static_cast<size_t>(m) * a.ldc + n] = v[j];
+      for (int q = 0; q < NQ; ++q) {
+        const int m = m0 + c + 4 * q + ew;
+        const int r0 = 4 * el;                 // first of 4 weight rows
+        if (a.mode == kEpiSwiGLU) {
+          // lanes 0..15 hold gate rows 0..63, lanes 16..31 the up rows of the same features
+          float4 up;
+          up.x = __shfl_down_sync(0xffffffffu, acc[q].x, 16);
+          up.y = __shfl_down_sync(0xffffffffu, acc[q].y, 16);
+          up.z = __shfl_down_sync(0xffffffffu, acc[q].z, 16);
+          up.w = __shfl_down_sync(0xffffffffu, acc[q].w, 16);
+          const int f = nt * 64 + r0;
+          if (el < 16 && m < a.M && f < (a.N >> 1) && a.vec_ok) {
+            bf16* C = reinterpret_cast<bf16*>(a.C) + static_cast<size_t>(m) * a.ldc + f;
+            uint2 pk;
+            pk.x = pack_bf16x2(silu(acc[q].x) * up.x, silu(acc[q].y) * up.y);
+            pk.y = pack_bf16x2(silu(acc[q].z) * up.z, silu(acc[q].w) * up.w);
+            *reinterpret_cast<uint2*>(C) = pk;
           }
         } else {
-          bf16* C = reinterpret_cast<bf16*>(a.C);
-#pragma unroll
-          for (int j = 0; j < CH; ++j) {
-            const int m = m0 + c + j;
-            if (m < a.M) {
-              float x = v[j];
-              if (a.residual != nullptr)
-                x += __bfloat162float(a.residual[static_cast<size_t>(m) * a.ldr + n]);
-              C[static_cast<size_t>(m) * a.ldc + n] = __float2bfloat16(x);
+          const int n = nt * BW + r0;
+          if (m < a.M && n < a.N) {
+            float vv[4] = {acc[q].x, acc[q].y, acc[q].z, acc[q].w};
+            if (a.mode == kEpiF32) {
+              float* C = reinterpret_cast<float*>(a.C) + static_cast<size_t>(m) * a.ldc;
+              if (n + 3 < a.N && a.vec_ok) {
+                *reinterpret_cast<float4*>(C + n) = acc[q];
+              } else {
+                for (int u = 0; u < 4 && n + u < a.N; ++u) C[n + u] = vv[u];
+              }
+            } else {
+              bf16* C = reinterpret_cast<bf16*>(a.C) + static_cast<size_t>(m) * a.ldc;
+              if (a.residual != nullptr) {
+                const bf16* R = a.residual + static_cast<size_t>(m) * a.ldr;
+                for (int u = 0; u < 4; ++u)
+                  if (n + u < a.N) vv[u] += __bfloat162float(R[n + u]);
+              }
+              if (n + 3 < a.N && a.vec_ok) {
+                uint2 pk;
+                pk.x = pack_bf16x2(vv[0], vv[1]);
+                pk.y = pack_bf16x2(vv[2], vv[3]);
+                *reinterpret_cast<uint2*>(C + n) = pk;
+              } else {
+                for (int u = 0; u < 4 && n + u < a.N; ++u) C[n + u] = __float2bfloat16(vv[u]);
+              }
             }
           }
         }
@@ -622,7 +655,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   // No CTA may leave while a peer still reads its shared memory.
+  if (tr && threadIdx.x == 64) tr[5] = globaltimer_ns();
   cluster_sync_all();
+  if (tr && threadIdx.x == 64) tr[6] = globaltimer_ns();
   if (*abort_flag) {
     if (warp == 0 && lane == 0) {
       for (int s = 0; s < STAGES; ++s)
@@ -810,7 +845,8 @@ static void launch_cluster(const CUtensorMap& tw, const CUtensorMap& tx, const G
 
 void gemm_bf16(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
                const c10::optional<at::Tensor>& residual, int64_t mode, at::Tensor& ws,
-               at::Tensor& counters, at::Tensor& err, int64_t bt, int64_t splits) {
+               at::Tensor& counters, at::Tensor& err, int64_t bt, int64_t splits,
+               const c10::optional<at::Tensor>& trace) {
   TORCH_CHECK(A.is_cuda() && W.is_cuda() && C.is_cuda(), "gemm: tensors must be CUDA");
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && W.scalar_type() == at::kBFloat16,
               "gemm: A and W must be bf16");
@@ -862,6 +898,11 @@ void gemm_bf16(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
   a.counters = sp > 1 ? counters.data_ptr<int>() : nullptr;
   a.mode = mode;
   a.err = err.data_ptr<int>();
+  a.vec_ok = (reinterpret_cast<uintptr_t>(C.data_ptr()) % 16 == 0) && (C.stride(0) % 4 == 0);
+  TORCH_CHECK(mode != kEpiSwiGLU || a.vec_ok, "swiglu gemm: C must be 16-byte aligned, ldc % 4 == 0");
+  a.trace = nullptr;
+  if (trace.has_value() && trace->defined())
+    a.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
 
   const CUtensorMap tw = make_tmap_bf16_2d(W.data_ptr(), K, N, W.stride(0) * 2, BK, BW,
                                            CU_TENSOR_MAP_SWIZZLE_128B);

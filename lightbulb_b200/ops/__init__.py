@@ -139,7 +139,8 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
     if a.is_cuda:
         C = _need_c()
         s = scratch(a.device)
-        C.gemm_bf16(a, w, out, residual, mode, s.gemm_ws, s.gemm_counters, s.err, bt, splits)
+        C.gemm_bf16(a, w, out, residual, mode, s.gemm_ws, s.gemm_counters, s.err, bt, splits,
+                    None)
         _launches[0] += 1
         return out
     # CPU restatement

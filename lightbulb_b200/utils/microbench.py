@@ -73,6 +73,32 @@ def bench_gemm(m, n, k, copies=None, mode=ops.EPI_STORE, bt=0, splits=0, iters=2
             "plan_bt_splits": plan[:2], "cublas_us": round(us_cublas, 2)}
 
 
+def trace_gemm(m, n, k, bt=0, splits=0):
+    """Per-CTA phase times (us) of one cluster split-K GEMM launch (globaltimer stamps)."""
+    from .. import _C
+    w = torch.randn(n, k, device="cuda").to(torch.bfloat16) * 0.02
+    a = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    s = ops.scratch(a.device)
+    tr = torch.zeros(4096 * 8, dtype=torch.int64, device="cuda")
+    for _ in range(3):
+        _C.gemm_bf16(a, w, out, None, 0, s.gemm_ws, s.gemm_counters, s.err, bt, splits, tr)
+    torch.cuda.synchronize()
+    t = tr.view(-1, 8).cpu()
+    t = t[t[:, 0] > 0].double()
+    t0 = t[:, 0].min()
+    names = ["start", "prologue", "acc_ready", "partial_staged", "cluster_sync1", "reduced",
+             "cluster_sync2"]
+    res = {"op": "gemm_trace", "m": m, "n": n, "k": k, "ctas": int(t.shape[0])}
+    for i, nm in enumerate(names):
+        col = t[:, i]
+        ok = col > 0
+        if ok.any():
+            res[nm + "_us"] = round(float((col[ok] - t0).mean()) / 1e3, 2)
+            res[nm + "_max_us"] = round(float((col[ok] - t0).max()) / 1e3, 2)
+    return res
+
+
 def bench_decode_attn(batch, ctx, hq, hkv, bs=16, splits=None, iters=20):
     bw, fl, src = peaks()
     d = 128
@@ -136,7 +162,7 @@ def bench_decode(batch, ctx, tp=1, model="llama3-8b"):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["decode", "gemm", "attn"])
+    ap.add_argument("what", choices=["decode", "gemm", "attn", "gemm_trace"])
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--ctx", type=int, default=1200)
     ap.add_argument("--tp", type=int, default=1)
@@ -152,6 +178,8 @@ def main(argv=None):
     torch.cuda.set_device(0)
     if a.what == "decode":
         rows = bench_decode(a.batch, a.ctx, a.tp, a.model)
+    elif a.what == "gemm_trace":
+        rows = [trace_gemm(a.m, a.n, a.k, a.bt, a.splits)]
     elif a.what == "gemm":
         rows = [bench_gemm(a.m, a.n, a.k, bt=a.bt, splits=a.splits)]
     else:
