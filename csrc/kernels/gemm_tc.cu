@@ -933,3 +933,171 @@ void gemm_bf16(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
 }
 
 }  // namespace lb
+
+// ======================================================================================
+// No-allocation entry point (declared in gemm_noalloc.h; no counterpart in the reference).
+// The persistent split-K kernel above, with its workspace, tile counters and error word in
+// one file-scope device array instead of caller- or allocator-provided memory.
+// ======================================================================================
+#include <cstdio>
+
+#include "gemm_noalloc.h"
+
+namespace {
+constexpr size_t kNaCounterWords = 16384;                    // per-tile arrival counters
+constexpr size_t kNaErrWords = 64;                           // error word (+ padding)
+constexpr size_t kNaHeadBytes = (kNaCounterWords + kNaErrWords) * sizeof(int);
+constexpr size_t kNaWsFloats = size_t(4) << 20;              // 16 MiB of fp32 partial tiles
+constexpr size_t kNaScratchBytes = kNaHeadBytes + kNaWsFloats * sizeof(float);
+constexpr int kNaMaxDevices = 64;
+}  // namespace
+
+// Shared by every call on a device; zero-initialised when the module loads.
+static __device__ __align__(256) unsigned char lb_gemm_noalloc_scratch[kNaScratchBytes];
+
+namespace {
+std::mutex na_mu;
+void* na_ptr[kNaMaxDevices] = {nullptr};
+
+template <int BT, int STAGES>
+cudaError_t na_launch(const CUtensorMap& tw, const CUtensorMap& tx, const lb::GemmArgs& a,
+                      int grid, cudaStream_t st) {
+  using L = lb::GemmSmem<BT, STAGES>;
+  lb::gemm_tc_kernel<BT, STAGES><<<grid, lb::kThreads, L::TOTAL, st>>>(tw, tx, a);
+  return cudaGetLastError();
+}
+
+template <int BT, int STAGES>
+cudaError_t na_set_attr() {
+  using L = lb::GemmSmem<BT, STAGES>;
+  return cudaFuncSetAttribute(lb::gemm_tc_kernel<BT, STAGES>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
+}
+
+int na_fail(int code, const char* msg, cudaError_t e = cudaSuccess) {
+  if (e != cudaSuccess)
+    std::fprintf(stderr, "lb_gemm_bf16_noalloc: %s: %s\n", msg, cudaGetErrorString(e));
+  else
+    std::fprintf(stderr, "lb_gemm_bf16_noalloc: %s\n", msg);
+  return code;
+}
+}  // namespace
+
+extern "C" int lb_gemm_bf16_noalloc(const void* A, int lda, const void* W, int ldw, void* C,
+                                    int ldc, int M, int N, int K, int splits,
+                                    cudaStream_t stream) {
+  using namespace lb;
+  if (!A || !W || !C || M <= 0 || N <= 0 || K <= 0 || splits < 1)
+    return na_fail(LB_NOALLOC_BAD_ARGS, "null pointer, non-positive size or splits < 1");
+  if (K % 8 != 0 || lda < K || ldw < K || ldc < N || (lda % 8) || (ldw % 8) ||
+      reinterpret_cast<uintptr_t>(A) % 16 || reinterpret_cast<uintptr_t>(W) % 16)
+    return na_fail(LB_NOALLOC_BAD_ARGS,
+                   "K, lda, ldw must be multiples of 8 elements and A, W 16-byte aligned");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return na_fail(LB_NOALLOC_CUDA_ERROR, "cudaGetDevice", e);
+  if (dev < 0 || dev >= kNaMaxDevices) return na_fail(LB_NOALLOC_BAD_ARGS, "device ordinal");
+
+  // One-time set-up per device (with that device current): scratch address + smem attribute.
+  void* base = nullptr;
+  {
+    std::lock_guard<std::mutex> g(na_mu);
+    if (na_ptr[dev] == nullptr) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, lb_gemm_noalloc_scratch);
+      if (e != cudaSuccess) return na_fail(LB_NOALLOC_CUDA_ERROR, "cudaGetSymbolAddress", e);
+      cudaError_t e2 = na_set_attr<16, 8>();
+      if (e2 == cudaSuccess) e2 = na_set_attr<32, 8>();
+      if (e2 == cudaSuccess) e2 = na_set_attr<64, 8>();
+      if (e2 == cudaSuccess) e2 = na_set_attr<128, 6>();
+      if (e2 == cudaSuccess) e2 = na_set_attr<256, 4>();
+      if (e2 != cudaSuccess) return na_fail(LB_NOALLOC_CUDA_ERROR, "cudaFuncSetAttribute", e2);
+      na_ptr[dev] = p;
+    }
+    base = na_ptr[dev];
+  }
+
+  const int BT = pick_bt(M);
+  const int m_tiles = (M + BT - 1) / BT;
+  const int n_tiles = (N + BW - 1) / BW;
+  const int kb_total = (K + BK - 1) / BK;
+  int sp = std::min(splits, kb_total);
+  const int kbps = (kb_total + sp - 1) / sp;
+  sp = (kb_total + kbps - 1) / kbps;
+  const size_t tiles = static_cast<size_t>(m_tiles) * n_tiles;
+  const size_t need = sp > 1 ? tiles * sp * BT * BW : 0;
+  if (need > kNaWsFloats || (sp > 1 && tiles > kNaCounterWords)) {
+    char msg[256];
+    std::snprintf(msg, sizeof(msg),
+                  "M=%d N=%d K=%d splits=%d needs %zu partial floats / %zu tiles; the static "
+                  "scratch holds %zu floats / %zu tiles",
+                  M, N, K, splits, need, tiles, kNaWsFloats, kNaCounterWords);
+    return na_fail(LB_NOALLOC_TOO_LARGE, msg);
+  }
+
+  int* counters = reinterpret_cast<int*>(base);
+  int* err = counters + kNaCounterWords;
+  float* ws = reinterpret_cast<float*>(static_cast<unsigned char*>(base) + kNaHeadBytes);
+  // Counters and the error word must start at zero: clear what this call uses.
+  e = cudaMemsetAsync(base, 0, kNaHeadBytes, stream);
+  if (e != cudaSuccess) return na_fail(LB_NOALLOC_CUDA_ERROR, "cudaMemsetAsync", e);
+
+  GemmArgs a;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.m_tiles = m_tiles;
+  a.n_tiles = n_tiles;
+  a.splits = sp;
+  a.kb_per_split = kbps;
+  a.kb_total = kb_total;
+  a.C = C;
+  a.ldc = ldc;
+  a.residual = nullptr;
+  a.ldr = 0;
+  a.ws = sp > 1 ? ws : nullptr;
+  a.counters = sp > 1 ? counters : nullptr;
+  a.mode = kEpiStore;
+  a.err = err;
+  a.trace = nullptr;
+  a.vec_ok = (reinterpret_cast<uintptr_t>(C) % 16 == 0) && (ldc % 4 == 0);
+
+  CUtensorMap tw, tx;
+  {
+    cuuint64_t dw[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
+    cuuint64_t sw[1] = {static_cast<cuuint64_t>(ldw) * 2};
+    cuuint32_t bw[2] = {BK, BW};
+    cuuint64_t dx[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+    cuuint64_t sx[1] = {static_cast<cuuint64_t>(lda) * 2};
+    cuuint32_t bx[2] = {BK, static_cast<cuuint32_t>(BT)};
+    cuuint32_t es[2] = {1, 1};
+    PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", reinterpret_cast<void**>(&enc),
+                                cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || enc == nullptr)
+      return na_fail(LB_NOALLOC_CUDA_ERROR, "cuTensorMapEncodeTiled unavailable", e);
+    CUresult r1 = enc(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(W), dw, sw, bw,
+                      es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r2 = enc(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(A), dx, sx, bx,
+                      es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS)
+      return na_fail(LB_NOALLOC_CUDA_ERROR, "cuTensorMapEncodeTiled failed");
+  }
+  int nsm = 0;
+  e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return na_fail(LB_NOALLOC_CUDA_ERROR, "cudaDeviceGetAttribute", e);
+  const int units = m_tiles * n_tiles * sp;
+  const int grid = std::min(units, nsm);
+  switch (BT) {
+    case 16: e = na_launch<16, 8>(tw, tx, a, grid, stream); break;
+    case 32: e = na_launch<32, 8>(tw, tx, a, grid, stream); break;
+    case 64: e = na_launch<64, 8>(tw, tx, a, grid, stream); break;
+    case 128: e = na_launch<128, 6>(tw, tx, a, grid, stream); break;
+    default: e = na_launch<256, 4>(tw, tx, a, grid, stream); break;
+  }
+  if (e != cudaSuccess) return na_fail(LB_NOALLOC_CUDA_ERROR, "kernel launch", e);
+  return LB_NOALLOC_OK;
+}
