@@ -97,7 +97,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
 }
 
 // ------------------------------------------------------------------------------------
-// TMA (cp.async.bulk.tensor), local global memory only.  No multicast anywhere.
+// TMA (cp.async.bulk.tensor): loads from this GPU's own global memory only.
 // ------------------------------------------------------------------------------------
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;

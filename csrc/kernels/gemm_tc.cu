@@ -19,7 +19,7 @@
 //    resets the counter for the next launch.
 //  * epilogues: bf16 store (+ residual add), fp32 store (logits), and SwiGLU on
 //    gate/up rows interleaved in 64-row groups (writes silu(g) * u, half width).
-//  * no cluster multicast: every TMA load reads this GPU's own memory.
+//  * every TMA load reads this GPU's own memory and fills one CTA's shared memory.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <cudaTypedefs.h>
@@ -382,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // its own shared memory (the drained pipeline buffers) and the tile is reduced through
 // distributed shared memory: CTA r sums every peer's partial for the 32-column chunks
 // c with c % S == r, in fixed rank order (deterministic), then runs the epilogue.  No
-// global workspace, no atomics, no multicast.
+// global workspace, no atomics.
 // ======================================================================================
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

@@ -83,7 +83,7 @@ class TPComm:
         rank.  Always all-gathers the shards (one collective, graph-capturable), then runs
         the device sampling kernel on the full rows."""
         b, vl = logits.shape
-        full = torch.empty(self.world, b, vl, dtype=logits.dtype, device=logits.device)
+        full = torch.empty(self.world * b, vl, dtype=logits.dtype, device=logits.device)
         dist.all_gather_into_tensor(full, logits.contiguous(), group=self.group)
-        full = full.permute(1, 0, 2).reshape(b, self.world * vl)
+        full = full.view(self.world, b, vl).permute(1, 0, 2).reshape(b, self.world * vl)
         ops.sample(full, temp, top_k, top_p, seeds, out_tokens)

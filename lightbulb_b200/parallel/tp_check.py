@@ -1,0 +1,68 @@
+"""Tensor-parallel self-check (run under torchrun, one process per GPU).
+
+    torchrun --nproc-per-node N -m lightbulb_b200.parallel.tp_check [--comm nccl|fused]
+
+Every rank builds the same random-init model sharded over the ranks and greedily generates;
+rank 0 also runs the unsharded model on its own GPU and compares.  Exit code 0 = match.
+"""
+from __future__ import annotations
+
+import argparse
+import sys
+
+import torch
+import torch.distributed as dist
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--comm", default="nccl", choices=["nccl", "fused"])
+    ap.add_argument("--graphs", type=int, default=1)
+    args = ap.parse_args(argv)
+    from ..config import CacheConfig, EngineConfig, SchedulerConfig, get_preset
+    from ..engine.llm_engine import LLMEngine
+    from ..engine.sampling import SamplingParams
+    from ..models.weights import pack_model, random_weights
+    from .comm import TPComm, init_distributed
+
+    rank, world, local = init_distributed(timeout_s=60)
+    dev = torch.device("cuda", local)
+    cfg = get_preset("tiny-test", hidden_size=1024, intermediate_size=2048, num_heads=8,
+                     num_kv_heads=8, head_dim=128, vocab_size=2048, num_layers=2)
+    w = random_weights(cfg, seed=11, std=0.05)
+    w = {k: v.to(torch.bfloat16).float() for k, v in w.items()}
+    comm = TPComm()
+    if args.comm == "fused":
+        from .fused import enable_fused
+        enable_fused(comm)
+
+    def engine(r, n, c):
+        packed = pack_model(cfg, w, rank=r, world=n, dtype=torch.bfloat16, device=dev)
+        ecfg = EngineConfig(model=cfg, cache=CacheConfig(num_blocks=128, block_size=16),
+                            scheduler=SchedulerConfig(max_num_seqs=8, max_num_batched_tokens=128,
+                                                      chunk_size=64, max_model_len=512),
+                            use_cuda_graphs=bool(args.graphs))
+        return LLMEngine(ecfg, packed, comm=c, tp_rank=r, tp_size=n)
+
+    prompts = [list(range(3, 80)), [5, 6, 7], [100] * 40]
+    sp = SamplingParams(temperature=0.0, max_tokens=10, ignore_eos=True)
+    eng = engine(rank, world, comm)
+    out = [s.output_token_ids for s in eng.generate(prompt_token_ids=prompts, params=sp)]
+    eng.runner.release_graphs()
+    ok = torch.tensor([1], device=dev)
+    if rank == 0:
+        ref_eng = engine(0, 1, None)
+        ref = [s.output_token_ids for s in ref_eng.generate(prompt_token_ids=prompts, params=sp)]
+        ref_eng.runner.release_graphs()
+        agree = sum(a[:4] == b[:4] for a, b in zip(out, ref))
+        print(f"tp{world} {args.comm}: {out}\nref: {ref}\nagree(first 4) {agree}/{len(ref)}",
+              flush=True)
+        ok[0] = int(agree == len(ref))
+    dist.broadcast(ok, 0)
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0 if int(ok.item()) == 1 else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())
