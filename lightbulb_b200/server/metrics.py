@@ -1,0 +1,64 @@
+"""Prometheus text exposition (``/metrics``) and the admin metrics snapshot.
+
+The reference's admin metrics return zeros (``src/api/admin.rs:184-194``); these come from
+the live engine: request/token counters, TTFT / ITL summaries, KV block usage, prefix-cache
+hit rate, speculative acceptance and step count.
+"""
+from __future__ import annotations
+
+import statistics
+import threading
+from typing import Dict, List
+
+
+def _q(vals: List[float], p: float) -> float:
+    if not vals:
+        return 0.0
+    s = sorted(vals)
+    return s[min(len(s) - 1, int(p * len(s)))]
+
+
+class Metrics:
+    def __init__(self):
+        self.lock = threading.Lock()
+        self.requests: Dict[str, int] = {}
+        self.errors = 0
+
+    def count(self, route: str):
+        with self.lock:
+            self.requests[route] = self.requests.get(route, 0) + 1
+
+    def snapshot(self, engine=None) -> dict:
+        d = {"requests": dict(self.requests), "errors": self.errors}
+        if engine is not None:
+            st = engine.stats
+            d.update({
+                "steps": st.steps, "prompt_tokens": st.prompt_tokens,
+                "generated_tokens": st.generated_tokens, "finished": st.finished,
+                "ttft_p50_s": _q(st.ttfts, 0.5), "ttft_p99_s": _q(st.ttfts, 0.99),
+                "itl_p50_s": _q(st.itls, 0.5), "itl_p99_s": _q(st.itls, 0.99),
+                "kv_blocks_total": engine.blocks.num_blocks,
+                "kv_blocks_free": engine.blocks.num_free_blocks(),
+                "kv_usage": engine.blocks.usage(),
+                "prefix_hit_rate": engine.blocks.prefix_hit_rate(),
+                "running": len(engine.scheduler.running),
+                "waiting": len(engine.scheduler.waiting),
+                "preemptions": engine.scheduler.num_preemptions,
+            })
+            if engine.spec is not None:
+                d["spec_acceptance"] = engine.spec.stats.acceptance_rate()
+        return d
+
+    def prometheus(self, engine=None) -> str:
+        s = self.snapshot(engine)
+        lines = []
+        for route, n in s["requests"].items():
+            lines.append(f'lb_requests_total{{route="{route}"}} {n}')
+        lines.append(f"lb_errors_total {s['errors']}")
+        for k in ("steps", "prompt_tokens", "generated_tokens", "finished", "ttft_p50_s",
+                  "ttft_p99_s", "itl_p50_s", "itl_p99_s", "kv_blocks_total", "kv_blocks_free",
+                  "kv_usage", "prefix_hit_rate", "running", "waiting", "preemptions",
+                  "spec_acceptance"):
+            if k in s:
+                lines.append(f"lb_{k} {s[k]}")
+        return "\n".join(lines) + "\n"
