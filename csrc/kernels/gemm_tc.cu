@@ -38,6 +38,23 @@ constexpr int kThreads = 192;  // warp 0: TMA, warp 1: MMA, warps 2..5: epilogue
 
 enum EpiMode : int { kEpiStore = 0, kEpiSwiGLU = 1, kEpiF32 = 2 };
 
+// Tensor-parallel link of a GEMM (all zero = plain GEMM).  Consumer side: the TMA producer
+// waits until *wait_flag >= wait_count (peers have pushed every row of the gathered input)
+// and the last CTA resets the flag.  Producer side (scatter): output row m goes to owner
+// o = m / rows_per_rank, into o's reduce-scatter slot for this rank, by P2P stores; the last
+// CTA then increments every owner's flag (system-scope release).
+struct TpLink {
+  bf16* scatter[8];
+  int* signal[8];
+  int world;
+  int rows_per_rank;
+  int src_rank;
+  long long slot_stride;  // elements between source slots in a receive buffer
+  int* wait_flag;
+  int wait_count;
+  int* done_counter;      // local grid-completion counter (reset by the last CTA)
+};
+
 struct GemmArgs {
   int M, N, K;
   int m_tiles, n_tiles, splits, kb_per_split, kb_total;
@@ -51,7 +68,31 @@ struct GemmArgs {
   int* err;
   unsigned long long* trace;  // optional: 8 globaltimer stamps per CTA (phase profiling)
   int vec_ok;                 // C base 16-byte aligned and ldc % 4 == 0: vector stores
+  TpLink tp;
 };
+
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_sys_add(int* p, int v) {
+  asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded wait for a flag written by peer GPUs (5 s budget).
+__device__ __forceinline__ bool wait_flag_geq(const int* flag, int target, volatile int* abort_flag) {
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t it = 0;
+  while (ld_acquire_sys(flag) < target) {
+    if ((++it & 63u) == 0) {
+      if (abort_flag != nullptr && *abort_flag) return false;
+      if (globaltimer_ns() - t0 > 5000000000ull) return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
+}
 
 template <int BT, int STAGES>
 struct GemmSmem {
@@ -411,6 +452,17 @@ __device__ __forceinline__ float4 ld_dsmem_f32x4(uint32_t addr) {
   return v;
 }
 
+// Destination row of output token m: local C, or (tensor-parallel scatter) the owner rank's
+// reduce-scatter receive slot for this source rank, reached by P2P stores over NVLink.
+__device__ __forceinline__ bf16* out_row(const GemmArgs& a, int m) {
+  if (a.tp.world > 0) {
+    const int o = m / a.tp.rows_per_rank;
+    const int r = m - o * a.tp.rows_per_rank;
+    return a.tp.scatter[o] + a.tp.src_rank * a.tp.slot_stride + static_cast<size_t>(r) * a.ldc;
+  }
+  return reinterpret_cast<bf16*>(a.C) + static_cast<size_t>(m) * a.ldc;
+}
+
 template <int BT, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_cluster_kernel(const __grid_constant__ CUtensorMap tmW,
@@ -481,7 +533,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t px = policy_evict_last();
       int stage = 0;
       uint32_t phase = 0;
-      for (int kb = kb0; kb < kb1; ++kb) {
+      if (a.tp.wait_flag != nullptr) {
+        if (!wait_flag_geq(a.tp.wait_flag, a.tp.wait_count, abort_flag)) {
+          record_error(a.err, kErrTimeoutPeer);
+          *abort_flag = 1;
+        }
+        // peers' rows were observed through the generic proxy; TMA reads via the async proxy
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+      }
+      for (int kb = kb0; kb < kb1 && !*abort_flag; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
           record_error(a.err, kErrTimeoutSmemEmpty);
           *abort_flag = 1;
@@ -615,7 +675,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           up.w = __shfl_down_sync(0xffffffffu, acc[q].w, 16);
           const int f = nt * 64 + r0;
           if (el < 16 && m < a.M && f < (a.N >> 1) && a.vec_ok) {
-            bf16* C = reinterpret_cast<bf16*>(a.C) + static_cast<size_t>(m) * a.ldc + f;
+            bf16* C = out_row(a, m) + f;
             uint2 pk;
             pk.x = pack_bf16x2(silu(acc[q].x) * up.x, silu(acc[q].y) * up.y);
             pk.y = pack_bf16x2(silu(acc[q].z) * up.z, silu(acc[q].w) * up.w);
@@ -633,7 +693,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int u = 0; u < 4 && n + u < a.N; ++u) C[n + u] = vv[u];
               }
             } else {
-              bf16* C = reinterpret_cast<bf16*>(a.C) + static_cast<size_t>(m) * a.ldc;
+              bf16* C = out_row(a, m);
               if (a.residual != nullptr) {
                 const bf16* R = a.residual + static_cast<size_t>(m) * a.ldr;
                 for (int u = 0; u < 4; ++u)
@@ -654,10 +714,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  if (a.tp.done_counter != nullptr) __threadfence_system();  // scatter stores before signal
   // No CTA may leave while a peer still reads its shared memory.
   if (tr && threadIdx.x == 64) tr[5] = globaltimer_ns();
   cluster_sync_all();
   if (tr && threadIdx.x == 64) tr[6] = globaltimer_ns();
+  if (a.tp.done_counter != nullptr && threadIdx.x == 0) {
+    // Grid completion: the last CTA resets the consumed input flag and signals the owners.
+    __threadfence_system();
+    const int prev = atomicAdd(a.tp.done_counter, 1);
+    if (prev == static_cast<int>(gridDim.x) - 1) {
+      __threadfence_system();
+      if (a.tp.wait_flag != nullptr) atomicExch(a.tp.wait_flag, 0);
+      for (int o = 0; o < a.tp.world; ++o)
+        if (a.tp.signal[o] != nullptr) red_release_sys_add(a.tp.signal[o], 1);
+      atomicExch(a.tp.done_counter, 0);
+    }
+  }
   if (*abort_flag) {
     if (warp == 0 && lane == 0) {
       for (int s = 0; s < STAGES; ++s)
@@ -875,7 +948,7 @@ void gemm_bf16(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
   const int nsplit = sp < 0 ? S : sp;
   const int kbps = (kb_total + nsplit - 1) / nsplit;
 
-  GemmArgs a;
+  GemmArgs a = {};
   a.M = M;
   a.N = N;
   a.K = K;
@@ -929,6 +1002,73 @@ void gemm_bf16(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
     case 128: launch_bt<128, 6>(tw, tx, a, grid, st); break;
     case 256: launch_bt<256, 4>(tw, tx, a, grid, st); break;
     default: TORCH_CHECK(false, "gemm: unsupported token tile ", BT);
+  }
+}
+
+}  // namespace lb
+
+namespace lb {
+// Tensor-parallel GEMM (decode shapes): cluster split-K kernel with a consumer wait on the
+// gathered-input flag and/or a scatter epilogue into the owners' reduce-scatter slots.
+// Pointers to peer memory come from CUDA IPC handles opened by the caller.
+void gemm_bf16_tp(const at::Tensor& A, const at::Tensor& W, at::Tensor& C, int64_t mode,
+                  at::Tensor& err, int64_t splits, std::vector<int64_t> scatter_ptrs,
+                  std::vector<int64_t> signal_ptrs, int64_t rows_per_rank, int64_t src_rank,
+                  int64_t slot_stride, int64_t wait_flag_ptr, int64_t wait_count,
+                  int64_t done_counter_ptr) {
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && W.scalar_type() == at::kBFloat16, "bf16");
+  TORCH_CHECK(A.stride(1) == 1 && W.stride(1) == 1 && C.stride(1) == 1, "inner stride 1");
+  const int M = A.size(0), K = A.size(1), N = W.size(0);
+  TORCH_CHECK(W.size(1) == K && K % 8 == 0, "gemm_tp: K");
+  TORCH_CHECK(scatter_ptrs.size() <= 8 && signal_ptrs.size() <= 8, "gemm_tp: world <= 8");
+  TORCH_CHECK(mode != kEpiF32 || scatter_ptrs.empty(), "gemm_tp: scatter is bf16 only");
+  if (M == 0) return;
+  const int BT = pick_bt(M);
+  const int m_tiles = (M + BT - 1) / BT, n_tiles = (N + BW - 1) / BW;
+  const int kb_total = (K + BK - 1) / BK;
+  int S = splits > 0 ? static_cast<int>(splits) : pick_cluster(BT, m_tiles * n_tiles, kb_total);
+  S = std::max(1, std::min(S, std::min(8, kb_total)));
+  GemmArgs a = {};
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.m_tiles = m_tiles;
+  a.n_tiles = n_tiles;
+  a.splits = 1;
+  a.kb_per_split = (kb_total + S - 1) / S;
+  a.kb_total = kb_total;
+  a.C = C.data_ptr();
+  a.ldc = C.stride(0);
+  a.mode = mode;
+  a.err = err.data_ptr<int>();
+  a.vec_ok = (reinterpret_cast<uintptr_t>(C.data_ptr()) % 16 == 0) && (C.stride(0) % 4 == 0);
+  a.tp.world = static_cast<int>(scatter_ptrs.size());
+  for (size_t i = 0; i < scatter_ptrs.size(); ++i)
+    a.tp.scatter[i] = reinterpret_cast<bf16*>(scatter_ptrs[i]);
+  for (size_t i = 0; i < signal_ptrs.size(); ++i)
+    a.tp.signal[i] = reinterpret_cast<int*>(signal_ptrs[i]);
+  if (a.tp.world > 0) {
+    TORCH_CHECK(signal_ptrs.size() == scatter_ptrs.size(), "gemm_tp: one flag per owner");
+    TORCH_CHECK(a.vec_ok, "gemm_tp: scatter needs 16-byte aligned rows");
+  }
+  a.tp.rows_per_rank = static_cast<int>(rows_per_rank);
+  a.tp.src_rank = static_cast<int>(src_rank);
+  a.tp.slot_stride = slot_stride;
+  a.tp.wait_flag = reinterpret_cast<int*>(wait_flag_ptr);
+  a.tp.wait_count = static_cast<int>(wait_count);
+  a.tp.done_counter = reinterpret_cast<int*>(done_counter_ptr);
+  TORCH_CHECK(a.tp.done_counter != nullptr, "gemm_tp: needs a completion counter");
+  const CUtensorMap tw = make_tmap_bf16_2d(W.data_ptr(), K, N, W.stride(0) * 2, BK, BW,
+                                           CU_TENSOR_MAP_SWIZZLE_128B);
+  const CUtensorMap tx = make_tmap_bf16_2d(A.data_ptr(), K, M, A.stride(0) * 2, BK, BT,
+                                           CU_TENSOR_MAP_SWIZZLE_128B);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  switch (BT) {
+    case 16: launch_cluster<16, 8>(tw, tx, a, S, st); break;
+    case 32: launch_cluster<32, 8>(tw, tx, a, S, st); break;
+    case 64: launch_cluster<64, 8>(tw, tx, a, S, st); break;
+    case 128: launch_cluster<128, 6>(tw, tx, a, S, st); break;
+    default: launch_cluster<256, 4>(tw, tx, a, S, st); break;
   }
 }
 
@@ -1042,7 +1182,7 @@ extern "C" int lb_gemm_bf16_noalloc(const void* A, int lda, const void* W, int l
   e = cudaMemsetAsync(base, 0, kNaHeadBytes, stream);
   if (e != cudaSuccess) return na_fail(LB_NOALLOC_CUDA_ERROR, "cudaMemsetAsync", e);
 
-  GemmArgs a;
+  GemmArgs a = {};
   a.M = M;
   a.N = N;
   a.K = K;

@@ -94,9 +94,13 @@ class ModelRunner:
         self.block_size = kv.block_size
         self.max_blocks_per_seq = (max_model_len + self.block_size - 1) // self.block_size + 1
         self.use_graphs = use_cuda_graphs and self.is_cuda
-        self.buckets = sorted(b for b in graph_buckets if b <= max_num_seqs) or [max_num_seqs]
+        step = comm.world if (comm is not None and getattr(comm, "fused_requested", False)) else 1
+        # fused tensor-parallel decode needs T % world == 0: round buckets up to multiples
+        bk = sorted({((b + step - 1) // step) * step for b in graph_buckets if b <= max_num_seqs})
+        top = ((max_num_seqs + step - 1) // step) * step
+        self.buckets = bk or [top]
         if self.buckets[-1] < max_num_seqs:
-            self.buckets.append(max_num_seqs)
+            self.buckets.append(top)
         self.graphs: Dict[int, _GraphBucket] = {}
         self.graph_pool = None
         self.comm = comm

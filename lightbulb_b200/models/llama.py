@@ -107,8 +107,51 @@ class LlamaModel:
         self.vocab_local = packed["lm_head"].shape[0]
 
     # ------------------------------------------------------------------------------
+    def fused_ok(self, b: ForwardBatch) -> bool:
+        c = self.comm
+        if c is None or c.world <= 1 or not getattr(c, "fused_requested", False):
+            return False
+        if self.device.type != "cuda":
+            return False
+        T = b.num_tokens
+        return (b.num_decode == len(b.cu_q) - 1 == T and T % c.world == 0 and
+                T <= getattr(c, "fused_max_rows", 512) and b.logits_idx.numel() == T)
+
+    def forward_fused(self, b: ForwardBatch, kv: KVCache) -> torch.Tensor:
+        """Decode step with GEMM + reduce-scatter + residual + RMSNorm + all-gather fused over
+        NVLink peer memory (see :mod:`lightbulb_b200.parallel.fused`)."""
+        from ..parallel.fused import ensure_fused
+        cfg = self.cfg
+        F = ensure_fused(self.comm, cfg.hidden_size, self.device)
+        T = b.num_tokens
+        R = T // F.world
+        r0 = F.rank * R
+        hq, hkv, d = self.hq, self.hkv, self.d
+        eps = cfg.rms_norm_eps
+        x = F.residual[:R]
+        ops.embedding(b.input_ids[r0:r0 + R], self.w["embed"], out=x)
+        F.norm_gather(self.layers[0]["ln_in"], R, eps, x_in=x, add_residual=False)
+        h = F.gather[:T]
+        attn = torch.empty(T, hq * d, dtype=torch.bfloat16, device=self.device)
+        for i, L in enumerate(self.layers):
+            qkv = F.gemm_consume(h, L["qkv"])
+            ops.rope_kv(qkv, b.positions, b.slots, self.cos_sin, kv.k[i], kv.v[i], hq, hkv)
+            q = qkv[:, :hq * d].view(T, hq, d)
+            ops.paged_attention(q, kv.k[i], kv.v[i], b.block_tables, b.seq_lens, b.cu_q,
+                                attn.view(T, hq, d), self.group, decode=True,
+                                num_splits=b.decode_splits)
+            F.gemm_scatter(attn, L["o"], R)
+            F.norm_gather(L["ln_post"], R, eps)
+            act = F.gemm_consume(h, L["gate_up"], mode=ops.EPI_SWIGLU)
+            F.gemm_scatter(act, L["down"], R)
+            nw = self.layers[i + 1]["ln_in"] if i + 1 < len(self.layers) else self.w["norm"]
+            F.norm_gather(nw, R, eps)
+        return F.gemm_consume(h, self.w["lm_head"], mode=ops.EPI_F32)
+
     def forward(self, b: ForwardBatch, kv: KVCache) -> torch.Tensor:
         """Returns fp32 logits [len(b.logits_idx), vocab_local]."""
+        if self.fused_ok(b):
+            return self.forward_fused(b, kv)
         cfg = self.cfg
         T = b.num_tokens
         hq, hkv, d = self.hq, self.hkv, self.d
