@@ -1,0 +1,106 @@
+"""Per-op timing of the tensor-parallel decode hot path (run under torchrun, one GPU per rank).
+
+    torchrun --nproc-per-node N -m lightbulb_b200.parallel.tp_bench [--tokens 256]
+
+For one Llama-3-8B layer shard it times, with CUDA events and the max over ranks:
+  nccl : o_proj GEMM -> NCCL all_reduce -> fused add+RMSNorm -> gate_up GEMM
+  fused: o_proj GEMM with scatter epilogue -> reduce+residual+RMSNorm+all-gather kernel ->
+         gate_up GEMM waiting on the gather flag
+and the pieces separately, so each collective's cost and the fused path's roofline fraction
+(the slower of compute at peak and bytes over NVLink at the measured 770 GB/s) are visible.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+
+import torch
+import torch.distributed as dist
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--tokens", type=int, default=256)
+    ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--hidden", type=int, default=4096)
+    ap.add_argument("--ffn", type=int, default=14336)
+    ap.add_argument("--heads", type=int, default=32)
+    a = ap.parse_args(argv)
+    from .. import ops
+    from .comm import TPComm, init_distributed
+    from .fused import enable_fused, ensure_fused
+    rank, world, local = init_distributed(timeout_s=60)
+    dev = torch.device("cuda", local)
+    comm = TPComm()
+    enable_fused(comm, max_rows=max(512, a.tokens))
+    F = ensure_fused(comm, a.hidden, dev)
+    T, H = a.tokens, a.hidden
+    R = T // world
+    g = torch.Generator(device=dev).manual_seed(rank + 1)
+    qd = a.heads * 128 // world
+    Wo = (torch.randn(H, qd, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    Wgu = (torch.randn(2 * a.ffn // world, H, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    attn = torch.randn(T, qd, device=dev, generator=g).to(torch.bfloat16)
+    x = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
+    lnw = torch.ones(H, device=dev, dtype=torch.bfloat16)
+
+    def timed(fn, iters=a.iters):
+        for _ in range(5):
+            fn()
+        torch.cuda.synchronize()
+        comm.barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(iters):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        us = s.elapsed_time(e) / iters * 1e3
+        return comm.max_float(us)
+
+    res = {}
+    res["gemm_o_local_us"] = timed(lambda: ops.gemm(attn, Wo))
+    o = ops.gemm(attn, Wo)
+    res["nccl_allreduce_us"] = timed(lambda: dist.all_reduce(o))
+    res["rmsnorm_add_us"] = timed(lambda: ops.rmsnorm(o, lnw, 1e-5, residual=x))
+    h = ops.rmsnorm(o, lnw, 1e-5)
+    res["gemm_gateup_local_us"] = timed(lambda: ops.gemm(h, Wgu, mode=ops.EPI_SWIGLU))
+
+    def nccl_chain():
+        y = ops.gemm(attn, Wo)
+        dist.all_reduce(y)
+        hh = ops.rmsnorm(y, lnw, 1e-5, residual=x)
+        ops.gemm(hh, Wgu, mode=ops.EPI_SWIGLU)
+
+    res["nccl_chain_us"] = timed(nccl_chain)
+    F.residual[:R].copy_(x[rank * R:(rank + 1) * R])
+
+    def scatter_only():
+        F.gemm_scatter(attn, Wo, R)
+        F.norm_gather(lnw, R, 1e-5)
+
+    res["fused_scatter_plus_normgather_us"] = timed(scatter_only)
+
+    def fused_chain():
+        F.gemm_scatter(attn, Wo, R)
+        F.norm_gather(lnw, R, 1e-5)
+        F.gemm_consume(F.gather[:T], Wgu, mode=ops.EPI_SWIGLU)
+
+    res["fused_chain_us"] = timed(fused_chain)
+    ops.check_errors(dev)
+    # roofline of the fused o_proj+RS: compute vs NVLink bytes leaving this rank
+    flops = 2 * T * qd * H
+    nvl = (world - 1) / world * T * H * 2 * 2   # scatter partials out + gathered rows out
+    res["fused_roofline_us"] = max(flops / 1.6424e15, nvl / 770e9) * 1e6
+    res["tokens"], res["world"] = T, world
+    if rank == 0:
+        print(json.dumps({k: (round(v, 2) if isinstance(v, float) else v) for k, v in res.items()}))
+    F.close()
+    comm.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
