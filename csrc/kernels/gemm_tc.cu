@@ -714,14 +714,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  if (a.tp.done_counter != nullptr) __threadfence_system();  // scatter stores before signal
   // No CTA may leave while a peer still reads its shared memory.
   if (tr && threadIdx.x == 64) tr[5] = globaltimer_ns();
   cluster_sync_all();
   if (tr && threadIdx.x == 64) tr[6] = globaltimer_ns();
   if (a.tp.done_counter != nullptr && threadIdx.x == 0) {
     // Grid completion: the last CTA resets the consumed input flag and signals the owners.
-    __threadfence_system();
+    // One system-scope fence per CTA, after the cluster barrier that ordered every thread's
+    // scatter stores before it (fences are cumulative), publishes this CTA's P2P stores.
+    if (a.tp.world > 0) __threadfence_system();
     const int prev = atomicAdd(a.tp.done_counter, 1);
     if (prev == static_cast<int>(gridDim.x) - 1) {
       __threadfence_system();

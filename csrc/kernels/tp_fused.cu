@@ -139,9 +139,11 @@ __global__ void __launch_bounds__(256) rs_norm_ag_kernel(const Args a) {
         reinterpret_cast<uint4*>(a.gather[d] + grow * a.H)[vi] = outv;
     }
   }
-  __threadfence_system();
+  // One system-scope fence per CTA, after the barrier that ordered all threads' gather
+  // stores before it (cumulative), then the grid-completion count.
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();
     const int prev = atomicAdd(a.done_counter, 1);
     if (prev == static_cast<int>(gridDim.x) - 1) {
       __threadfence_system();

@@ -45,18 +45,35 @@ def main(argv=None) -> int:
     x = torch.randn(T, H, device=dev, generator=g).to(torch.bfloat16)
     lnw = torch.ones(H, device=dev, dtype=torch.bfloat16)
 
-    def timed(fn, iters=a.iters):
-        for _ in range(5):
+    def timed(fn, iters=a.iters, reps=10):
+        """Device time per call: ``reps`` calls captured in one CUDA graph, replayed ``iters``
+        times between CUDA events (no host launch overhead), max over ranks."""
+        for _ in range(3):
             fn()
         torch.cuda.synchronize()
         comm.barrier()
+        graph = torch.cuda.CUDAGraph()
+        st = torch.cuda.Stream()
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            fn()
+        torch.cuda.current_stream().wait_stream(st)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph):
+            for _ in range(reps):
+                fn()
+        torch.cuda.synchronize()
+        comm.barrier()
+        graph.replay()
+        torch.cuda.synchronize()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
         for _ in range(iters):
-            fn()
+            graph.replay()
         e.record()
         torch.cuda.synchronize()
-        us = s.elapsed_time(e) / iters * 1e3
+        us = s.elapsed_time(e) / (iters * reps) * 1e3
+        del graph
         return comm.max_float(us)
 
     res = {}
