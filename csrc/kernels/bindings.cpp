@@ -22,7 +22,7 @@ void gemm_bf16_tp(const at::Tensor& A, const at::Tensor& W, at::Tensor& C, int64
                   at::Tensor& err, int64_t splits, std::vector<int64_t> scatter_ptrs,
                   std::vector<int64_t> signal_ptrs, int64_t rows_per_rank, int64_t src_rank,
                   int64_t slot_stride, int64_t wait_flag_ptr, int64_t wait_count,
-                  int64_t done_counter_ptr);
+                  int64_t done_counter_ptr, int64_t trace_ptr);
 int64_t ipc_alloc(int64_t bytes);
 void ipc_free(int64_t ptr);
 at::Tensor ipc_export(int64_t ptr);
@@ -32,7 +32,7 @@ void rs_norm_ag(int64_t rs_ptr, const c10::optional<at::Tensor>& x_in, at::Tenso
                 const at::Tensor& w, std::vector<int64_t> gather_ptrs,
                 std::vector<int64_t> gather_flag_ptrs, int64_t rs_flag_ptr,
                 int64_t done_counter_ptr, int64_t rank, int64_t R, int64_t rows, double eps,
-                bool add_residual, at::Tensor& err);
+                bool add_residual, at::Tensor& err, int64_t trace_ptr);
 void embedding(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, at::Tensor& err);
 void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w,
              at::Tensor& y, double eps);
@@ -53,13 +53,22 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_plan", &lb::gemm_plan, "token tile, split-K and workspace size of a GEMM");
   m.def("paged_attention", &lb::paged_attention, "paged attention (decode / prefill)");
   m.def("paged_decode_tma", &lb::paged_decode_tma, "TMA-fed warp-specialised paged decode");
-  m.def("gemm_bf16_tp", &lb::gemm_bf16_tp, "tensor-parallel GEMM (wait / scatter / signal)");
+  m.def("gemm_bf16_tp", &lb::gemm_bf16_tp, "tensor-parallel GEMM (wait / scatter / signal)",
+        py::arg("A"), py::arg("W"), py::arg("C"), py::arg("mode"), py::arg("err"),
+        py::arg("splits"), py::arg("scatter_ptrs"), py::arg("signal_ptrs"),
+        py::arg("rows_per_rank"), py::arg("src_rank"), py::arg("slot_stride"),
+        py::arg("wait_flag_ptr"), py::arg("wait_count"), py::arg("done_counter_ptr"),
+        py::arg("trace_ptr") = 0);
   m.def("ipc_alloc", &lb::ipc_alloc);
   m.def("ipc_free", &lb::ipc_free);
   m.def("ipc_export", &lb::ipc_export);
   m.def("ipc_open", &lb::ipc_open);
   m.def("ipc_close", &lb::ipc_close);
-  m.def("rs_norm_ag", &lb::rs_norm_ag, "reduce-scatter sum + residual + RMSNorm + all-gather");
+  m.def("rs_norm_ag", &lb::rs_norm_ag, "reduce-scatter sum + residual + RMSNorm + all-gather",
+        py::arg("rs_ptr"), py::arg("x_in"), py::arg("residual"), py::arg("w"),
+        py::arg("gather_ptrs"), py::arg("gather_flag_ptrs"), py::arg("rs_flag_ptr"),
+        py::arg("done_counter_ptr"), py::arg("rank"), py::arg("R"), py::arg("rows"),
+        py::arg("eps"), py::arg("add_residual"), py::arg("err"), py::arg("trace_ptr") = 0);
   m.def("embedding", &lb::embedding, "embedding gather");
   m.def("rmsnorm", &lb::rmsnorm, "RMSNorm with optional fused residual add");
   m.def("rope_kv", &lb::rope_kv, "RoPE + paged KV append");

@@ -730,6 +730,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int o = 0; o < a.tp.world; ++o)
         if (a.tp.signal[o] != nullptr) red_release_sys_add(a.tp.signal[o], 1);
       atomicExch(a.tp.done_counter, 0);
+      if (a.trace) a.trace[4095 * 8 + 7] = globaltimer_ns();
     }
   }
   if (*abort_flag) {
@@ -1016,7 +1017,7 @@ void gemm_bf16_tp(const at::Tensor& A, const at::Tensor& W, at::Tensor& C, int64
                   at::Tensor& err, int64_t splits, std::vector<int64_t> scatter_ptrs,
                   std::vector<int64_t> signal_ptrs, int64_t rows_per_rank, int64_t src_rank,
                   int64_t slot_stride, int64_t wait_flag_ptr, int64_t wait_count,
-                  int64_t done_counter_ptr) {
+                  int64_t done_counter_ptr, int64_t trace_ptr) {
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && W.scalar_type() == at::kBFloat16, "bf16");
   TORCH_CHECK(A.stride(1) == 1 && W.stride(1) == 1 && C.stride(1) == 1, "inner stride 1");
   const int M = A.size(0), K = A.size(1), N = W.size(0);
@@ -1058,6 +1059,7 @@ void gemm_bf16_tp(const at::Tensor& A, const at::Tensor& W, at::Tensor& C, int64
   a.tp.wait_flag = reinterpret_cast<int*>(wait_flag_ptr);
   a.tp.wait_count = static_cast<int>(wait_count);
   a.tp.done_counter = reinterpret_cast<int*>(done_counter_ptr);
+  a.trace = reinterpret_cast<unsigned long long*>(trace_ptr);
   TORCH_CHECK(a.tp.done_counter != nullptr, "gemm_tp: needs a completion counter");
   const CUtensorMap tw = make_tmap_bf16_2d(W.data_ptr(), K, N, W.stride(0) * 2, BK, BW,
                                            CU_TENSOR_MAP_SWIZZLE_128B);

@@ -46,6 +46,7 @@ struct Args {
   int world, rank, R, rows, H, mode, add_residual;
   float eps;
   int* err;
+  unsigned long long* trace;  // optional: CTA 0 stamps [start, flag seen, pushed, signalled]
 };
 
 template <int VPT>
@@ -53,6 +54,8 @@ __global__ void __launch_bounds__(256) rs_norm_ag_kernel(const Args a) {
   const int row = blockIdx.x;  // local row index < rows
   __shared__ int s_ok;
   __shared__ float red[32];
+  unsigned long long* tr = (a.trace != nullptr && blockIdx.x == 0) ? a.trace : nullptr;
+  if (tr && threadIdx.x == 0) tr[0] = globaltimer_ns();
   if (threadIdx.x == 0) {
     int ok = 1;
     if (a.mode == 0) {
@@ -68,6 +71,7 @@ __global__ void __launch_bounds__(256) rs_norm_ag_kernel(const Args a) {
       }
     }
     s_ok = ok;
+    if (tr) tr[1] = globaltimer_ns();
   }
   __syncthreads();
   const int nvec = a.H / 8;
@@ -143,6 +147,7 @@ __global__ void __launch_bounds__(256) rs_norm_ag_kernel(const Args a) {
   // stores before it (cumulative), then the grid-completion count.
   __syncthreads();
   if (threadIdx.x == 0) {
+    if (tr) tr[2] = globaltimer_ns();
     __threadfence_system();
     const int prev = atomicAdd(a.done_counter, 1);
     if (prev == static_cast<int>(gridDim.x) - 1) {
@@ -150,6 +155,7 @@ __global__ void __launch_bounds__(256) rs_norm_ag_kernel(const Args a) {
       if (a.mode == 0) atomicExch(a.rs_flag, 0);
       for (int d = 0; d < a.world; ++d) red_release_sys_add(a.gather_flag[d], 1);
       atomicExch(a.done_counter, 0);
+      if (a.trace) a.trace[3] = globaltimer_ns();
     }
   }
 }
@@ -193,8 +199,9 @@ void rs_norm_ag(int64_t rs_ptr, const c10::optional<at::Tensor>& x_in, at::Tenso
                 const at::Tensor& w, std::vector<int64_t> gather_ptrs,
                 std::vector<int64_t> gather_flag_ptrs, int64_t rs_flag_ptr,
                 int64_t done_counter_ptr, int64_t rank, int64_t R, int64_t rows, double eps,
-                bool add_residual, at::Tensor& err) {
+                bool add_residual, at::Tensor& err, int64_t trace_ptr) {
   tpf::Args a = {};
+  a.trace = reinterpret_cast<unsigned long long*>(trace_ptr);
   a.world = static_cast<int>(gather_ptrs.size());
   TORCH_CHECK(a.world >= 1 && a.world <= 8 && gather_flag_ptrs.size() == gather_ptrs.size(),
               "rs_norm_ag: world");

@@ -93,18 +93,35 @@ def main(argv=None) -> int:
     res["nccl_chain_us"] = timed(nccl_chain)
     F.residual[:R].copy_(x[rank * R:(rank + 1) * R])
 
-    def scatter_only():
-        F.gemm_scatter(attn, Wo, R)
-        F.norm_gather(lnw, R, 1e-5)
-
-    res["fused_scatter_plus_normgather_us"] = timed(scatter_only)
-
     def fused_chain():
         F.gemm_scatter(attn, Wo, R)
         F.norm_gather(lnw, R, 1e-5)
         F.gemm_consume(F.gather[:T], Wgu, mode=ops.EPI_SWIGLU)
 
     res["fused_chain_us"] = timed(fused_chain)
+    # one traced chain (globaltimer stamps, ns relative to this rank's GEMM start)
+    tr_g = torch.zeros(4096 * 8, dtype=torch.int64, device=dev)
+    tr_n = torch.zeros(8, dtype=torch.int64, device=dev)
+    torch.cuda.synchronize()
+    comm.barrier()
+    F.C.gemm_bf16_tp(attn, Wo, F._row_shape, ops.EPI_STORE, F.err, 0, F.rs_peers,
+                     F.rs_flag_peers, R, rank, R * H, 0, 0, F.done, tr_g.data_ptr())
+    F.C.rs_norm_ag(F.rs_peers[rank], None, F.residual[:R], lnw, F.g_peers, F.g_flag_peers,
+                   F.rs_flag, F.done, rank, R, R, 1e-5, True, F.err, tr_n.data_ptr())
+    F.gemm_consume(F.gather[:T], Wgu, mode=ops.EPI_SWIGLU)
+    torch.cuda.synchronize()
+    g = tr_g.view(-1, 8).cpu()
+    g0 = int(g[g[:, 0] > 0, 0].min())
+    n = tr_n.cpu().tolist()
+    trace = {"gemm_acc_ready_max": int(g[g[:, 2] > 0, 2].max()) - g0,
+             "gemm_reduced_max": int(g[g[:, 5] > 0, 5].max()) - g0,
+             "gemm_signal": int(g[-1, 7]) - g0,
+             "norm_start": n[0] - g0, "norm_flag_seen": n[1] - g0, "norm_pushed": n[2] - g0,
+             "norm_signal": n[3] - g0}
+    res["trace_ns_rank%d" % rank] = trace
+    tall = [None] * world
+    dist.all_gather_object(tall, trace)
+    res["trace_ns_all"] = tall
     ops.check_errors(dev)
     # roofline of the fused o_proj+RS: compute vs NVLink bytes leaving this rank
     flops = 2 * T * qd * H
