@@ -79,6 +79,11 @@ __device__ __forceinline__ int ld_acquire_sys(const int* p) {
 __device__ __forceinline__ void red_release_sys_add(int* p, int v) {
   asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+// Release/acquire fence at system scope: enough to publish prior (and cumulatively
+// observed) stores before a flag update; lighter than the sequentially-consistent fence.
+__device__ __forceinline__ void fence_acq_rel_sys() {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
 
 // Bounded wait for a flag written by peer GPUs (5 s budget).
 __device__ __forceinline__ bool wait_flag_geq(const int* flag, int target, volatile int* abort_flag) {
@@ -722,10 +727,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Grid completion: the last CTA resets the consumed input flag and signals the owners.
     // One system-scope fence per CTA, after the cluster barrier that ordered every thread's
     // scatter stores before it (fences are cumulative), publishes this CTA's P2P stores.
-    if (a.tp.world > 0) __threadfence_system();
+    if (a.tp.world > 0) fence_acq_rel_sys();
     const int prev = atomicAdd(a.tp.done_counter, 1);
     if (prev == static_cast<int>(gridDim.x) - 1) {
-      __threadfence_system();
+      fence_acq_rel_sys();
       if (a.tp.wait_flag != nullptr) atomicExch(a.tp.wait_flag, 0);
       for (int o = 0; o < a.tp.world; ++o)
         if (a.tp.signal[o] != nullptr) red_release_sys_add(a.tp.signal[o], 1);

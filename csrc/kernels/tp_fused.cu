@@ -33,6 +33,11 @@ __device__ __forceinline__ int ld_acquire_sys(const int* p) {
 __device__ __forceinline__ void red_release_sys_add(int* p, int v) {
   asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+// Release/acquire fence at system scope: enough to publish prior (and cumulatively
+// observed) stores before a flag update; lighter than the sequentially-consistent fence.
+__device__ __forceinline__ void fence_acq_rel_sys() {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
 
 struct Args {
   const bf16* rs;          // local receive buffer [world][R][H]
@@ -148,10 +153,10 @@ __global__ void __launch_bounds__(256) rs_norm_ag_kernel(const Args a) {
   __syncthreads();
   if (threadIdx.x == 0) {
     if (tr) tr[2] = globaltimer_ns();
-    __threadfence_system();
+    fence_acq_rel_sys();
     const int prev = atomicAdd(a.done_counter, 1);
     if (prev == static_cast<int>(gridDim.x) - 1) {
-      __threadfence_system();
+      fence_acq_rel_sys();
       if (a.mode == 0) atomicExch(a.rs_flag, 0);
       for (int d = 0; d < a.world; ++d) red_release_sys_add(a.gather_flag[d], 1);
       atomicExch(a.done_counter, 0);
