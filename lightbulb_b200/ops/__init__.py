@@ -236,21 +236,15 @@ def rope_kv(qkv: torch.Tensor, positions: torch.Tensor, slots: Optional[torch.Te
 # ------------------------------------------------------------------------------------
 def decode_splits(num_seqs: int, num_kv_heads: int, max_kv_len: int, sms: int = 148,
                   ctas_per_sm: int = 2) -> int:
-    """Split-KV factor for decode: the split count (each split >= 256 keys, <= 32 splits)
-    whose CTA count wastes the least of its last wave of ``sms * ctas_per_sm`` slots."""
+    """Split-KV factor for decode.  Splitting only pays when the (sequence, KV head) CTAs
+    cannot fill one wave of ``sms * ctas_per_sm`` slots (measured: at 512 CTAs a 4-way split
+    is 1.6x slower than none); then split so the CTAs cover the slots, each split keeping
+    >= 512 keys."""
     ctas = num_seqs * num_kv_heads
     slots = sms * ctas_per_sm
-    if ctas == 0 or ctas >= 4 * slots:
+    if ctas == 0 or ctas >= slots:
         return 1
-    max_s = max(1, min(32, max_kv_len // 256))
-    best, best_eff = 1, 0.0
-    for s in range(1, max_s + 1):
-        n = ctas * s
-        waves = (n + slots - 1) // slots
-        eff = n / (waves * slots)
-        if eff > best_eff + 0.03:
-            best, best_eff = s, eff
-    return best
+    return max(1, min(32, (slots + ctas - 1) // ctas, max(1, max_kv_len // 512)))
 
 
 def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
