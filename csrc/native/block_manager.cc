@@ -187,7 +187,7 @@ class BlockManager {
     seqs_[child] = std::move(c);
   }
 
-  // Drop the last `n` token slots of `sid` (speculative decoding rollback).
+  // Keep the first `new_len` token slots of `sid` (speculative decoding rollback).
   void truncate(int64_t sid, int64_t new_len) {
     auto& s = get(sid);
     if (new_len >= s.num_tokens) return;
@@ -195,6 +195,16 @@ class BlockManager {
     while (static_cast<int64_t>(s.blocks.size()) > keep_blocks) {
       release(s.blocks.back());
       s.blocks.pop_back();
+    }
+    // A kept, partially truncated block will be written again: if it is published in the
+    // prefix index (for the tokens that were cut), withdraw it so no later lookup splices
+    // KV that is about to change.  A shared block is copied on write instead.
+    if (new_len % block_size_ != 0 && !s.blocks.empty()) {
+      const int b = s.blocks.back();
+      if (is_cached_[b] && ref_[b] == 1) {
+        index_.erase(cached_key_[b]);
+        is_cached_[b] = 0;
+      }
     }
     s.num_tokens = new_len;
     if (static_cast<int64_t>(s.tokens.size()) > new_len) s.tokens.resize(new_len);

@@ -152,6 +152,16 @@ class LLMEngine:
         self.stats.prompt_tokens += len(prompt_token_ids)
         return seq
 
+    def attach_draft(self, draft_packed: dict, draft_cfg, k: int = 4, **kw):
+        """Enable speculative decoding with a draft model (same tokenizer / vocabulary)."""
+        from ..models.llama import LlamaModel
+        from .speculative import attach_speculative
+        dm = LlamaModel(draft_cfg, draft_packed, self.model.tp_rank, self.model.tp_size,
+                        max_positions=self.cfg.scheduler.max_model_len + k + 64,
+                        comm=self.model.comm)
+        return attach_speculative(self, dm, draft_cfg, k=k,
+                                  use_cuda_graphs=self.cfg.use_cuda_graphs, **kw)
+
     def abort(self, request_id: str) -> None:
         self.scheduler.abort(request_id)
 

@@ -105,14 +105,16 @@ class ModelRunner:
         self.graph_pool = None
         self.comm = comm
         pin = self.is_cuda
-        n_int = 4 * self.max_tokens + 3 * (max_num_seqs + 1) + max_num_seqs * self.max_blocks_per_seq
+        n_int = 6 * self.max_tokens + 3 * (max_num_seqs + 1) + max_num_seqs * self.max_blocks_per_seq
         self.h_ints = torch.zeros(n_int, dtype=torch.int32, pin_memory=pin)
-        self.h_floats = torch.zeros(2 * max_num_seqs + 2, dtype=torch.float32, pin_memory=pin)
-        self.h_seeds = torch.zeros(max_num_seqs + 1, dtype=torch.int64, pin_memory=pin)
-        self.h_out = torch.zeros(max_num_seqs + 1, dtype=torch.int32, pin_memory=pin)
+        # sampled rows per step: one per sequence, or every row of a verify chunk
+        ns = self.max_tokens + 1
+        self.h_floats = torch.zeros(2 * ns, dtype=torch.float32, pin_memory=pin)
+        self.h_seeds = torch.zeros(ns, dtype=torch.int64, pin_memory=pin)
+        self.h_out = torch.zeros(ns, dtype=torch.int32, pin_memory=pin)
         self.d_ints = torch.zeros(n_int, dtype=torch.int32, device=self.device)
-        self.d_floats = torch.zeros(2 * max_num_seqs + 2, dtype=torch.float32, device=self.device)
-        self.d_seeds = torch.zeros(max_num_seqs + 1, dtype=torch.int64, device=self.device)
+        self.d_floats = torch.zeros(2 * ns, dtype=torch.float32, device=self.device)
+        self.d_seeds = torch.zeros(ns, dtype=torch.int64, device=self.device)
         self.h2d_bytes = 0
         self.d2h_bytes = 0
         self._events = None  # list of (start, end) CUDA events per step when enabled
@@ -163,12 +165,17 @@ class ModelRunner:
             if not c.needs_logits:
                 continue
             p = c.seq.params
-            temps.append(p.temperature)
-            topk.append(p.top_k)
-            topp.append(p.top_p)
-            # greedy rows never read their seed: skip the hash
-            seeds.append(token_seed(c.seq.request_id, len(c.seq.output_token_ids), p.seed)
-                         if p.temperature > 0 else 0)
+            rows = c.num_tokens if c.logits_all else 1
+            # row i samples output token number len(outputs) + i (a verify chunk's rows are
+            # the positions after each of its input tokens)
+            base = len(c.seq.output_token_ids)
+            for i in range(rows):
+                temps.append(p.temperature)
+                topk.append(p.top_k)
+                topp.append(p.top_p)
+                # greedy rows never read their seed: skip the hash
+                seeds.append(token_seed(c.seq.request_id, base + i, p.seed)
+                             if p.temperature > 0 else 0)
         return temps, topk, topp, seeds
 
     # -------------------------------------------------------------------------------
@@ -282,7 +289,7 @@ class ModelRunner:
 
         ids, pos, slots = take(T), take(T), take(T)
         seq_lens, cu_q = take(B), take(B + 1)
-        nlog = sum(1 for c in chunks if c.needs_logits)
+        nlog = sum((c.num_tokens if c.logits_all else 1) for c in chunks if c.needs_logits)
         logits_idx = take(nlog)
         top_k = take(nlog)
         bt = take(B * width).reshape(B, width)
@@ -300,8 +307,12 @@ class ModelRunner:
             seq_lens[i] = c.start + n
             cu_q[i + 1] = t
             if c.needs_logits:
-                logits_idx[li] = t - 1
-                li += 1
+                if c.logits_all:
+                    logits_idx[li:li + n] = np.arange(t - n, t, dtype=np.int32)
+                    li += n
+                else:
+                    logits_idx[li] = t - 1
+                    li += 1
         self._fill_block_tables([c.seq for c in chunks], bt, width)
         temps, tk, tp, seeds = self._sampling_rows(chunks)
         top_k[:] = tk

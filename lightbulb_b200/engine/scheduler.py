@@ -36,6 +36,7 @@ class ScheduledChunk:
     num_tokens: int     # tokens fed this step
     slots: List[int]
     needs_logits: bool  # chunk reaches the end of the known tokens -> sample
+    logits_all: bool = False  # sample every row of the chunk (speculative verify)
 
 
 @dataclass
