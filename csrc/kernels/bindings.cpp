@@ -33,6 +33,10 @@ void rs_norm_ag(int64_t rs_ptr, const c10::optional<at::Tensor>& x_in, at::Tenso
                 std::vector<int64_t> gather_flag_ptrs, int64_t rs_flag_ptr,
                 int64_t done_counter_ptr, int64_t rank, int64_t R, int64_t rows, double eps,
                 bool add_residual, at::Tensor& err, int64_t trace_ptr);
+void h2o_accumulate(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& block_tables,
+                    const at::Tensor& seq_lens, at::Tensor& score, double decay);
+void kv_compact(at::Tensor& storage, const at::Tensor& src, const at::Tensor& dst,
+                const c10::optional<at::Tensor>& score);
 void embedding(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, at::Tensor& err);
 void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w,
              at::Tensor& y, double eps);
@@ -69,6 +73,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("gather_ptrs"), py::arg("gather_flag_ptrs"), py::arg("rs_flag_ptr"),
         py::arg("done_counter_ptr"), py::arg("rank"), py::arg("R"), py::arg("rows"),
         py::arg("eps"), py::arg("add_residual"), py::arg("err"), py::arg("trace_ptr") = 0);
+  m.def("h2o_accumulate", &lb::h2o_accumulate, "H2O decayed attention-mass accumulation");
+  m.def("kv_compact", &lb::kv_compact, "copy kept KV token slots (all layers)");
   m.def("embedding", &lb::embedding, "embedding gather");
   m.def("rmsnorm", &lb::rmsnorm, "RMSNorm with optional fused residual add");
   m.def("rope_kv", &lb::rope_kv, "RoPE + paged KV append");

@@ -212,6 +212,14 @@ class BlockManager {
     if (static_cast<int64_t>(s.hashes.size()) > full) s.hashes.resize(full);
   }
 
+  // Fresh blocks owned by the caller (refcount 1), e.g. compaction targets.
+  std::vector<int> alloc_blocks(int n) {
+    if (n > num_free_blocks()) throw std::runtime_error("out of KV blocks");
+    std::vector<int> out;
+    for (int i = 0; i < n; ++i) out.push_back(take_free());
+    return out;
+  }
+
   // Replace the table of `sid` with a compacted list of kept logical blocks (KV eviction:
   // the caller has moved surviving slots); blocks not kept are released.
   void set_blocks(int64_t sid, const std::vector<int>& blocks, int64_t num_tokens) {
@@ -398,6 +406,7 @@ void register_block_manager(py::module_& m) {
       .def("fork", &BlockManager::fork)
       .def("truncate", &BlockManager::truncate)
       .def("set_blocks", &BlockManager::set_blocks)
+      .def("alloc_blocks", &BlockManager::alloc_blocks)
       .def("free_sequence", &BlockManager::free_sequence)
       .def("block_table", &BlockManager::block_table)
       .def("num_tokens", &BlockManager::num_tokens)

@@ -105,6 +105,12 @@ class LLMEngine:
         self.kv_policy = None  # KV compression policy (kv/compression.py) when configured
         log.info("engine ready: %d KV blocks of %d tokens (%.1f GiB)", nb, cfg.cache.block_size,
                  self.kv.storage.numel() * 2 / 2**30)
+        if cfg.cache.h2o_budget > 0:
+            self.enable_kv_compression("h2o", cfg.cache.h2o_budget, cfg.cache.sink_tokens,
+                                       decay=cfg.cache.h2o_decay)
+        elif cfg.cache.streaming_window > 0:
+            self.enable_kv_compression("streaming", cfg.cache.streaming_window,
+                                       cfg.cache.sink_tokens)
 
     # ---------------------------------------------------------------------------------
     @classmethod
@@ -175,8 +181,22 @@ class LLMEngine:
         so = self.scheduler.schedule()
         if so.empty:
             return []
+        if self.kv_policy is not None and hasattr(self.kv_policy, "before_step"):
+            self.kv_policy.before_step(so)
         res = self.runner.execute(so)
         return self._process(res.chunks, res.tokens)
+
+    def enable_kv_compression(self, kind: str = "h2o", budget: int = 2048, sinks: int = 4,
+                              **kw):
+        """H2O heavy hitters (budget + sinks tokens kept) or StreamingLLM (sinks + window)."""
+        from ..kv.compression import H2OPolicy, StreamingPolicy
+        if kind == "h2o":
+            self.kv_policy = H2OPolicy(self, budget=budget, sinks=sinks, **kw)
+        elif kind == "streaming":
+            self.kv_policy = StreamingPolicy(self, sinks=sinks, window=budget)
+        else:
+            raise ValueError(kind)
+        return self.kv_policy
 
     def _process(self, chunks, tokens) -> List[RequestOutput]:
         now = time.perf_counter()

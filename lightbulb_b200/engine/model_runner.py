@@ -212,7 +212,7 @@ class ModelRunner:
         for i, c in enumerate(chunks):
             s = c.seq
             ids[i] = s.last_token
-            pos[i] = c.start
+            pos[i] = c.start + getattr(s, "evicted", 0)
             slots[i] = c.slots[0]
             seq_lens[i] = c.start + 1
         cu_q[:B + 1] = np.arange(B + 1, dtype=np.int32)
@@ -300,8 +300,9 @@ class ModelRunner:
         for i, c in enumerate(chunks):
             s = c.seq
             n = c.num_tokens
-            ids[t:t + n] = s.all_token_ids[c.start:c.start + n]
-            pos[t:t + n] = np.arange(c.start, c.start + n, dtype=np.int32)
+            t0 = c.start + getattr(s, "evicted", 0)   # token index (KV index + evicted)
+            ids[t:t + n] = s.all_token_ids[t0:t0 + n]
+            pos[t:t + n] = np.arange(t0, t0 + n, dtype=np.int32)
             slots[t:t + n] = c.slots
             t += n
             seq_lens[i] = c.start + n

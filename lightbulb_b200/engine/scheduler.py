@@ -114,6 +114,7 @@ class Scheduler:
         victim = self.running.pop()
         self.blocks.free_sequence(victim.seq_id)
         victim.num_computed_tokens = 0
+        victim.evicted = 0  # compressed KV is rebuilt from the full token list
         victim.status = SeqStatus.WAITING
         victim.preemptions += 1
         self.waiting.appendleft(victim)
@@ -204,8 +205,9 @@ class Scheduler:
         return out
 
     def _prefill_chunk(self, seq: Sequence, n: int, out: SchedulerOutput) -> ScheduledChunk:
-        start = seq.num_computed_tokens
-        toks = seq.all_token_ids[start:start + n]
+        start = seq.num_computed_tokens          # KV index
+        t0 = start + seq.evicted                 # token index
+        toks = seq.all_token_ids[t0:t0 + n]
         slots, cow = self.blocks.append_slots(seq.seq_id, n, toks)
         out.cow_pairs += cow
-        return ScheduledChunk(seq, start, n, slots, start + n == seq.num_tokens)
+        return ScheduledChunk(seq, start, n, slots, t0 + n == seq.num_tokens)

@@ -45,6 +45,7 @@ class Sequence:
     max_new_tokens: int = 0          # budget after context truncation
     truncated: bool = False
     preemptions: int = 0
+    evicted: int = 0                 # tokens dropped from the KV cache (compression)
     # speculative decoding
     spec_draft_tokens: List[int] = field(default_factory=list)
 
@@ -80,7 +81,7 @@ class Sequence:
     @property
     def num_uncomputed(self) -> int:
         """Tokens still to feed through the model (1 in steady decode, more in prefill)."""
-        return self.num_tokens - self.num_computed_tokens
+        return self.num_tokens - self.evicted - self.num_computed_tokens
 
     @property
     def is_prefilling(self) -> bool:

@@ -104,6 +104,7 @@ class LlamaModel:
         mp = max_positions or cfg.max_position_embeddings
         self.cos_sin = ops.rope_table(mp, cfg.head_dim, cfg.rope_theta, self.device)
         self.comm = comm  # tensor-parallel communicator (None = single GPU)
+        self.h2o = None   # H2O policy: accumulates last-layer attention mass (kv/compression.py)
         self.vocab_local = packed["lm_head"].shape[0]
 
     # ------------------------------------------------------------------------------
@@ -178,6 +179,8 @@ class LlamaModel:
                                     a3, self.group, decode=False, tile_seq=b.tile_seq,
                                     tile_row0=b.tile_row0, seq_lens_cpu=b.seq_lens_cpu,
                                     cu_q_cpu=b.cu_q_cpu)
+            if self.h2o is not None and nd > 0 and i == len(self.layers) - 1:
+                self.h2o.accumulate(q[:nd], kv.k[i], b.block_tables[:nd], b.seq_lens[:nd])
             o = ops.gemm(attn, L["o"])
             if comm is not None:
                 o = comm.all_reduce(o)
