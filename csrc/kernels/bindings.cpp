@@ -37,6 +37,9 @@ void h2o_accumulate(const at::Tensor& q, const at::Tensor& k_cache, const at::Te
                     const at::Tensor& seq_lens, at::Tensor& score, double decay);
 void kv_compact(at::Tensor& storage, const at::Tensor& src, const at::Tensor& dst,
                 const c10::optional<at::Tensor>& score);
+void gemm_quant(const at::Tensor& X, const at::Tensor& qw, const at::Tensor& scales,
+                const at::Tensor& offsets, int64_t bits, int64_t group, at::Tensor& C,
+                int64_t mode, int64_t splits, at::Tensor& err);
 void embedding(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, at::Tensor& err);
 void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w,
              at::Tensor& y, double eps);
@@ -75,6 +78,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("eps"), py::arg("add_residual"), py::arg("err"), py::arg("trace_ptr") = 0);
   m.def("h2o_accumulate", &lb::h2o_accumulate, "H2O decayed attention-mass accumulation");
   m.def("kv_compact", &lb::kv_compact, "copy kept KV token slots (all layers)");
+  m.def("gemm_quant", &lb::gemm_quant, "dequant-fused tcgen05 GEMM (int4 / int8 groups)");
   m.def("embedding", &lb::embedding, "embedding gather");
   m.def("rmsnorm", &lb::rmsnorm, "RMSNorm with optional fused residual add");
   m.def("rope_kv", &lb::rope_kv, "RoPE + paged KV append");

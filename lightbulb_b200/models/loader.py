@@ -89,13 +89,46 @@ def load_awq_weights(path: str):
     return cfg, w, quant, acfg
 
 
+def quantized_layers(cfg, fmt, path, quant=None, reader=None):
+    """HF-named projection -> QuantWeight for AWQ / GGUF Q4_K / Q8_0 checkpoints (None when
+    a projection is stored in another type; the caller then keeps the bf16 path)."""
+    from ..formats import quant as Q
+    out = {}
+    if fmt == "awq":
+        for base, (q, z, s) in quant.items():
+            out[base + ".weight"] = Q.from_awq(q, z, s, q.shape[1] // s.shape[1])
+        return out
+    from ..formats.gguf import GGML_Q4_K, GGML_Q8_0, gguf_name_to_hf
+    for name, (dims, t, _, _) in reader.tensors.items():
+        hf = gguf_name_to_hf(name)
+        if hf is None or not hf.endswith("_proj.weight"):
+            continue
+        n, k = dims[1], dims[0]
+        raw = reader.raw(name).numpy()
+        if t == GGML_Q8_0:
+            out[hf] = Q.from_q8_0(raw, n, k)
+        elif t == GGML_Q4_K:
+            out[hf] = Q.from_q4_k(raw, n, k)
+        else:
+            return None
+    return out
+
+
 def load_model_dir(path: str, device="cuda", tp_rank: int = 0, tp_size: int = 1,
-                   dtype=torch.bfloat16):
+                   dtype=torch.bfloat16, keep_quantized: Optional[bool] = None):
+    """``keep_quantized`` (default: on CUDA) keeps AWQ / GGUF Q4_K / Q8_0 projections in the
+    dequant-fused GEMM layout instead of dequantizing them to bf16 at load."""
     fmt = detect_format(path)
+    keep = (torch.device(device).type == "cuda") if keep_quantized is None else keep_quantized
+    qlayers = None
     if fmt == "gguf":
-        cfg, w, tok, _ = load_gguf_weights(path)
+        cfg, w, tok, reader = load_gguf_weights(path)
+        if keep:
+            qlayers = quantized_layers(cfg, fmt, path, reader=reader)
     elif fmt == "awq":
-        cfg, w, _, _ = load_awq_weights(path)
+        cfg, w, quant, _ = load_awq_weights(path)
+        if keep:
+            qlayers = quantized_layers(cfg, fmt, path, quant=quant)
         tok = None
     else:
         cfg, w = load_hf_weights(path)
@@ -107,4 +140,12 @@ def load_model_dir(path: str, device="cuda", tp_rank: int = 0, tp_size: int = 1,
             with open(os.path.join(path, "config.json")) as f:
                 tok = load_tokenizer(path, cfg.vocab_size, json.load(f))
     packed = pack_model(cfg, w, rank=tp_rank, world=tp_size, dtype=dtype, device=device)
+    if qlayers:
+        from .weights import pack_layer_quant
+        for i in range(cfg.num_layers):
+            lw = dict(qlayers)
+            p = f"model.layers.{i}."
+            for nm in ("input_layernorm.weight", "post_attention_layernorm.weight"):
+                lw[p + nm] = w[p + nm]
+            packed["layers"][i] = pack_layer_quant(cfg, lw, i, tp_rank, tp_size, device)
     return cfg, packed, tok

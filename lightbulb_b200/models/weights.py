@@ -215,3 +215,69 @@ def random_packed_model(cfg: ModelConfig, seed: int = 0, rank: int = 0, world: i
         "lm_head": lm[rank * vl:min(v, (rank + 1) * vl)].to(dtype).contiguous(),
         "layers": layers,
     }
+
+
+# ----------------------------------------------------------------------------------------
+# Quantized packing (AWQ int4 / GGUF Q4_K / Q8_0 -> dequant-fused GEMM layout)
+# ----------------------------------------------------------------------------------------
+def pack_layer_quant(cfg: ModelConfig, lw: Dict[str, object], i: int, rank: int = 0,
+                     world: int = 1, device="cpu") -> Dict[str, object]:
+    """``lw`` maps HF projection names to QuantWeight (norms as tensors)."""
+    from ..formats.quant import cat_rows, interleave_rows
+    p = f"model.layers.{i}."
+    d = cfg.head_dim
+    (q0, hq), (k0, hk) = tp_head_ranges(cfg, rank, world)
+    fl = cfg.intermediate_size // world
+    qw = lw[p + "self_attn.q_proj.weight"].rows(slice(q0 * d, (q0 + hq) * d))
+    kw = lw[p + "self_attn.k_proj.weight"].rows(slice(k0 * d, (k0 + hk) * d))
+    vw = lw[p + "self_attn.v_proj.weight"].rows(slice(k0 * d, (k0 + hk) * d))
+    ow = lw[p + "self_attn.o_proj.weight"].cols(q0 * d, (q0 + hq) * d)
+    gw = lw[p + "mlp.gate_proj.weight"].rows(slice(rank * fl, (rank + 1) * fl))
+    uw = lw[p + "mlp.up_proj.weight"].rows(slice(rank * fl, (rank + 1) * fl))
+    dw = lw[p + "mlp.down_proj.weight"].cols(rank * fl, (rank + 1) * fl)
+
+    def dev(t):
+        return t.contiguous().to(device)
+
+    def nrm(name):
+        return lw[p + name].to(device=device, dtype=torch.bfloat16).contiguous()
+
+    return {"ln_in": nrm("input_layernorm.weight"), "ln_post": nrm("post_attention_layernorm.weight"),
+            "qkv": dev(cat_rows([qw, kw, vw])), "o": dev(ow),
+            "gate_up": dev(interleave_rows(gw, uw)), "down": dev(dw)}
+
+
+def random_packed_awq_model(cfg: ModelConfig, seed: int = 0, rank: int = 0, world: int = 1,
+                            device="cuda", group: int = 128):
+    """Random AWQ int4 model (uint4 weights, fp16 scales U[0.001, 0.02], zeros U{0..15}),
+    created shard by shard on the device; norms / embeddings random bf16."""
+    from ..formats.quant import QuantWeight
+    g = torch.Generator(device=device).manual_seed(seed)
+    shapes = weight_shapes(cfg)
+    layers = []
+
+    def qlin(n, k):
+        qw = torch.randint(0, 256, (n, k // 2), generator=g, device=device, dtype=torch.int32)
+        s = torch.empty(n, k // group, device=device).uniform_(0.001, 0.02, generator=g)
+        z = torch.randint(0, 16, (n, k // group), generator=g, device=device).float()
+        return QuantWeight(qw.to(torch.uint8), s.half(), (z * s).half(), 4, group)
+
+    for i in range(cfg.num_layers):
+        p = f"model.layers.{i}."
+        lw = {}
+        for name in ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj",
+                     "self_attn.o_proj", "mlp.gate_proj", "mlp.up_proj", "mlp.down_proj"):
+            n_, k_ = shapes[p + name + ".weight"]
+            lw[p + name + ".weight"] = qlin(n_, k_)
+        for name in ("input_layernorm.weight", "post_attention_layernorm.weight"):
+            lw[p + name] = random_tensor(p + name, shapes[p + name], seed, torch.bfloat16, device)
+        layers.append(pack_layer_quant(cfg, lw, i, rank, world, device))
+    top = {n: random_tensor(n, shapes[n], seed, torch.bfloat16, device)
+           for n in ("model.embed_tokens.weight", "model.norm.weight", "lm_head.weight")
+           if n in shapes}
+    v = cfg.vocab_size
+    vl = (v + world - 1) // world
+    lm = top.get("lm_head.weight", top["model.embed_tokens.weight"])
+    return {"embed": top["model.embed_tokens.weight"].contiguous(),
+            "norm": top["model.norm.weight"].contiguous(),
+            "lm_head": lm[rank * vl:min(v, (rank + 1) * vl)].contiguous(), "layers": layers}

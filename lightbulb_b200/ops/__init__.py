@@ -128,6 +128,9 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
     """``out = a @ w.T`` (+ residual) with epilogue ``mode``:
     EPI_STORE -> bf16 [M, N]; EPI_F32 -> fp32 [M, N]; EPI_SWIGLU -> bf16 [M, N/2] of
     ``silu(gate) * up`` for gate/up rows interleaved in 64-row groups."""
+    from ..formats.quant import QuantWeight
+    if isinstance(w, QuantWeight):
+        return gemm_quant(a, w, out, mode, splits)
     m, n = a.shape[0], w.shape[0]
     if out is None:
         if mode == EPI_SWIGLU:
@@ -156,6 +159,25 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
             y = y + residual.float()
         out.copy_(y.to(out.dtype))
     return out
+
+
+def gemm_quant(a: torch.Tensor, w, out: Optional[torch.Tensor] = None, mode: int = EPI_STORE,
+               splits: int = 0) -> torch.Tensor:
+    """``a @ dequant(w).T`` for a :class:`~lightbulb_b200.formats.quant.QuantWeight`."""
+    m, n = a.shape[0], w.shape[0]
+    if out is None:
+        if mode == EPI_SWIGLU:
+            out = torch.empty(m, n // 2, dtype=torch.bfloat16, device=a.device)
+        elif mode == EPI_F32:
+            out = torch.empty(m, n, dtype=torch.float32, device=a.device)
+        else:
+            out = torch.empty(m, n, dtype=torch.bfloat16, device=a.device)
+    if a.is_cuda:
+        _need_c().gemm_quant(a, w.qw, w.scales, w.offsets, w.bits, w.group, out, mode,
+                             max(0, splits), scratch(a.device).err)
+        _launches[0] += 1
+        return out
+    return gemm(a, w.dequantize(torch.bfloat16), out, None, mode)
 
 
 def gemm_plan(m: int, n: int, k: int, bt: int = 0, splits: int = 0):

@@ -123,3 +123,19 @@ def test_loaders_safetensors_gguf_awq(tmp_path):
     assert detect_format(aw) == "awq"
     c3, p3, _ = load_model_dir(aw, device="cpu")
     assert len(_greedy(c3, p3)) == 6
+
+
+def test_awq_and_gguf_kept_quantized_match_dequantized(tmp_path):
+    from lightbulb_b200.formats.quant import QuantWeight
+    from lightbulb_b200.models.loader import load_model_dir
+    cfg = get_preset("tiny-test")
+    w = random_weights(cfg, seed=6, std=0.05)
+    aw = str(tmp_path / "awq")
+    A.save_awq_checkpoint(aw, cfg, w, group=128)
+    gg = str(tmp_path / "m.gguf")
+    G.save_llama_gguf(gg, cfg, w, linear_type=G.GGML_Q4_K)
+    for path in (aw, gg):
+        cq, pq, _ = load_model_dir(path, device="cpu", keep_quantized=True)
+        cd, pd, _ = load_model_dir(path, device="cpu", keep_quantized=False)
+        assert isinstance(pq["layers"][0]["qkv"], QuantWeight)
+        assert _greedy(cq, pq)[:3] == _greedy(cd, pd)[:3]
