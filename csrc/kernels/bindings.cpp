@@ -22,7 +22,8 @@ void gemm_bf16_tp(const at::Tensor& A, const at::Tensor& W, at::Tensor& C, int64
                   at::Tensor& err, int64_t splits, std::vector<int64_t> scatter_ptrs,
                   std::vector<int64_t> signal_ptrs, int64_t rows_per_rank, int64_t src_rank,
                   int64_t slot_stride, int64_t wait_flag_ptr, int64_t wait_count,
-                  int64_t done_counter_ptr, int64_t trace_ptr);
+                  int64_t done_counter_ptr, int64_t trace_ptr,
+                  const c10::optional<at::Tensor>& ws);
 int64_t ipc_alloc(int64_t bytes);
 void ipc_free(int64_t ptr);
 at::Tensor ipc_export(int64_t ptr);
@@ -39,7 +40,7 @@ void kv_compact(at::Tensor& storage, const at::Tensor& src, const at::Tensor& ds
                 const c10::optional<at::Tensor>& score);
 void gemm_quant(const at::Tensor& X, const at::Tensor& qw, const at::Tensor& scales,
                 const at::Tensor& offsets, int64_t bits, int64_t group, at::Tensor& C,
-                int64_t mode, int64_t splits, at::Tensor& err);
+                int64_t mode, int64_t splits, at::Tensor& err, at::Tensor& ws);
 void embedding(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, at::Tensor& err);
 void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w,
              at::Tensor& y, double eps);
@@ -65,7 +66,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("splits"), py::arg("scatter_ptrs"), py::arg("signal_ptrs"),
         py::arg("rows_per_rank"), py::arg("src_rank"), py::arg("slot_stride"),
         py::arg("wait_flag_ptr"), py::arg("wait_count"), py::arg("done_counter_ptr"),
-        py::arg("trace_ptr") = 0);
+        py::arg("trace_ptr") = 0, py::arg("ws") = py::none());
   m.def("ipc_alloc", &lb::ipc_alloc);
   m.def("ipc_free", &lb::ipc_free);
   m.def("ipc_export", &lb::ipc_export);

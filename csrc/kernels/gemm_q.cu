@@ -22,6 +22,7 @@
 #include <cudaTypedefs.h>
 #include <torch/extension.h>
 
+#include "cluster_rs.cuh"
 #include "common.cuh"
 
 namespace lb {
@@ -40,6 +41,7 @@ struct Args {
   int mode;  // 0 bf16, 1 swiglu, 2 fp32
   int vec_ok;
   int* err;
+  float* ws;  // split-K exchange workspace (cluster_rs.cuh)
 };
 
 template <int BT, int STAGES, int QBITS>
@@ -53,42 +55,16 @@ struct Smem {
   static constexpr int TOTAL = BAR_OFF + 512 + 1024;
 };
 
-__device__ __forceinline__ uint32_t ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t nctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
-}
-__device__ __forceinline__ uint32_t mapa(uint32_t saddr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ float4 ld_dsmem4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr)
-               : "memory");
-  return v;
-}
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 
 template <int BT, int STAGES, int QBITS>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmX,
-                  const Args a) {
+                  const __grid_constant__ CUtensorMap tmC, const Args a) {
   using L = Smem<BT, STAGES, QBITS>;
   constexpr int CH = L::CH;
   constexpr int TMEM_COLS = BT < 32 ? 32 : BT;
-  static_assert(BW * BT * 4 <= STAGES * L::STAGE, "partial must fit");
+  static_assert(crs::smem_bytes(BT, 2) <= STAGES * L::STAGE, "split-K slots");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -96,20 +72,23 @@ __global__ void __launch_bounds__(THREADS, 1)
   auto sW = [&](int s) { return smem + s * L::STAGE; };
   auto sX = [&](int s) { return smem + s * L::STAGE + L::W_BYTES; };
   auto sQ = [&](int s) { return smem + s * L::STAGE + L::W_BYTES + L::X_BYTES; };
-  float* sPart = reinterpret_cast<float*>(smem);
+  float* sSlots = reinterpret_cast<float*>(smem);  // after the main loop: split-K slots
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
   uint64_t* full = bars;
   uint64_t* ready = bars + STAGES;
   uint64_t* empty = bars + 2 * STAGES;
   uint64_t* tfull = bars + 3 * STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
+  uint64_t* rbar = tfull + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* s_go = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t S = nctarank(), rank = ctarank();
+  const uint32_t S = crs::nctarank(), rank = crs::ctarank();
+  uint8_t* sOut = smem + crs::num_slots(BT, S) * crs::SLOT_BYTES;  // output staging
   const int tile = blockIdx.x / S;
   const int mt = tile % a.m_tiles, nt = tile / a.m_tiles;
+  float* ws_tile = a.ws + crs::ws_floats(tile, BT, S);
   const int kb0 = rank * a.kb_per_split;
   const int kb1 = min(kb0 + a.kb_per_split, a.kb_total);
 
@@ -120,6 +99,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(tfull, 1);
+    mbar_init(rbar, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -190,7 +170,35 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int gpr = a.K / a.group;     // groups per weight row
     int stage = 0;
     uint32_t phase = 0;
+    // Scale / offset of the (at most two) groups a 64-wide k-block touches, prefetched one
+    // k-block ahead so the global-load latency overlaps the wait and the previous dequant.
+    const __half* srow = a.scales + static_cast<size_t>(n < a.N ? n : 0) * gpr;
+    const __half* orow = a.offsets + static_cast<size_t>(n < a.N ? n : 0) * gpr;
+    // Dequantisation without int->float conversions (magic-number method): a value q held
+    // in the low mantissa bits of bf16 128.0 (0x4300 | q) or fp32 2^23 (0x4B000000 | b)
+    // reads as 128 + q or 2^23 + b exactly; widening bf16 -> fp32 is a shift.  4-bit: one
+    // FMA with the offset pre-folded as o + 128 s (128 s is exact; the fold's rounding is
+    // ~1e-5 s, far below bf16 output precision).  8-bit: 2^23 + 128 is subtracted first
+    // (exact), since folding 2^23 s into the offset would cost half a quantisation step.
+    //  4-bit words (repacked offline): bits [4i, 4i+4) = element 2i, bits [16+4i, 20+4i) =
+    //  element 2i+1, so (w >> 4i) & 0x000F000F | 0x43004300 is the bf16 pair (2i, 2i+1).
+    //  8-bit bytes are stored biased (q + 128).
+    auto fetch = [&](int kb, float& s0, float& o0, float& s1, float& o1) {
+      const int g0 = (kb * BK) / a.group, g1 = (kb * BK + 32) / a.group;
+      s0 = __half2float(__ldg(srow + g0));
+      o0 = __half2float(__ldg(orow + g0));
+      s1 = __half2float(__ldg(srow + g1));
+      o1 = __half2float(__ldg(orow + g1));
+      if constexpr (QBITS == 4) {
+        o0 += 128.f * s0;
+        o1 += 128.f * s1;
+      }
+    };
+    float ns0 = 0.f, no0 = 0.f, ns1 = 0.f, no1 = 0.f;
+    if (kb0 < kb1) fetch(kb0, ns0, no0, ns1, no1);
     for (int kb = kb0; kb < kb1; ++kb) {
+      const float cs0 = ns0, co0 = no0, cs1 = ns1, co1 = no1;
+      if (kb + 1 < kb1) fetch(kb + 1, ns0, no0, ns1, no1);
       int go = 1;
       if (!mbar_wait(&full[stage], phase, abort_flag)) {
         record_error(a.err, kErrTimeoutTmaFull);
@@ -199,46 +207,42 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       go = __all_sync(0xffffffffu, go);
       if (!go) break;
-      // 64 values of row `row` at k = kb*64 .. +63
-      float v[64];
+      uint8_t* wdst = sW(stage) + row * 128;
       if constexpr (QBITS == 4) {
         const uint4* src = reinterpret_cast<const uint4*>(sQ(stage) + row * 32);
         const uint4 p0 = src[0], p1 = src[1];
         const uint32_t w[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+        for (int c = 0; c < 8; ++c) {  // word c = elements 8c .. 8c+7 = output chunk c
+          const float sc = c < 4 ? cs0 : cs1, of = c < 4 ? co0 : co1;
+          uint32_t o[4];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) v[i * 8 + j] = static_cast<float>((w[i] >> (4 * j)) & 0xF);
+          for (int i = 0; i < 4; ++i) {
+            const uint32_t t = ((w[c] >> (4 * i)) & 0x000F000Fu) | 0x43004300u;
+            const float lo = __uint_as_float(t << 16), hi = __uint_as_float(t & 0xFFFF0000u);
+            o[i] = pack_bf16x2(fmaf(lo, sc, -of), fmaf(hi, sc, -of));
+          }
+          *reinterpret_cast<uint4*>(wdst + ((c ^ (row & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
       } else {
         const uint4* src = reinterpret_cast<const uint4*>(sQ(stage) + row * 64);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint4 p = src[i];
-          const uint32_t w[4] = {p.x, p.y, p.z, p.w};
+        for (int c = 0; c < 8; ++c) {  // 8 bytes = elements 8c .. 8c+7
+          const uint4 p = src[c >> 1];
+          const uint32_t w0 = (c & 1) ? p.z : p.x, w1 = (c & 1) ? p.w : p.y;
+          const float sc = c < 4 ? cs0 : cs1, of = c < 4 ? co0 : co1;
+          uint32_t o[4];
 #pragma unroll
-          for (int t = 0; t < 4; ++t)
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              v[i * 16 + t * 4 + j] = static_cast<float>(static_cast<int8_t>((w[t] >> (8 * j)) & 0xFF));
+          for (int i = 0; i < 4; ++i) {
+            const uint32_t ww = i < 2 ? w0 : w1;
+            const int b = (i & 1) * 2;
+            const float x0 = __uint_as_float(__byte_perm(ww, 0x4B000000u, 0x7650 + b)) - 8388736.f;
+            const float x1 =
+                __uint_as_float(__byte_perm(ww, 0x4B000000u, 0x7650 + b + 1)) - 8388736.f;
+            o[i] = pack_bf16x2(fmaf(x0, sc, -of), fmaf(x1, sc, -of));
+          }
+          *reinterpret_cast<uint4*>(wdst + ((c ^ (row & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
         }
-      }
-      // per-group scale / offset (group >= 32 divides 64 or is a multiple of it)
-      const int k0 = kb * BK;
-      uint8_t* wdst = sW(stage) + row * 128;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {  // 16-byte chunk c holds k0 + 8c .. +7
-        const int g = (k0 + c * 8) / a.group;
-        float sc = 0.f, of = 0.f;
-        if (n < a.N) {
-          sc = __half2float(a.scales[static_cast<size_t>(n) * gpr + g]);
-          of = __half2float(a.offsets[static_cast<size_t>(n) * gpr + g]);
-        }
-        uint4 outv;
-        outv.x = pack_bf16x2(v[c * 8 + 0] * sc - of, v[c * 8 + 1] * sc - of);
-        outv.y = pack_bf16x2(v[c * 8 + 2] * sc - of, v[c * 8 + 3] * sc - of);
-        outv.z = pack_bf16x2(v[c * 8 + 4] * sc - of, v[c * 8 + 5] * sc - of);
-        outv.w = pack_bf16x2(v[c * 8 + 6] * sc - of, v[c * 8 + 7] * sc - of);
-        *reinterpret_cast<uint4*>(wdst + ((c ^ (row & 7)) << 4)) = outv;
       }
       // generic-proxy smem writes -> visible to the tensor core (async proxy)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -249,8 +253,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         phase ^= 1u;
       }
     }
-    // ---- accumulator -> own shared-memory partial ----
-    const int quad = warp & 3, trow = quad * 32 + lane;
+    // ---- accumulator ready: publish the partial tile ----
     if (row == 0) {
       int gg = 1;
       if (kb1 <= kb0) gg = 2;
@@ -262,93 +265,30 @@ __global__ void __launch_bounds__(THREADS, 1)
       s_go[0] = gg;
     }
     named_bar_sync(1, 128);
-    if (s_go[0] == 1) {
-      tc_fence_after();
-      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
-#pragma unroll 1
-      for (int c = 0; c < BT; c += CH) {
-        uint32_t r[CH];
-        if constexpr (CH == 32) tmem_ld32(tbase + c, *reinterpret_cast<uint32_t(*)[32]>(r));
-        else tmem_ld16(tbase + c, *reinterpret_cast<uint32_t(*)[16]>(r));
-        tc_wait_ld();
-#pragma unroll
-        for (int j = 0; j < CH; ++j) sPart[(c + j) * BW + trow] = __uint_as_float(r[j]);
-      }
-    } else {
-      for (int c = 0; c < BT; ++c) sPart[c * BW + trow] = 0.f;
-    }
+    tc_fence_after();
+    const int quad = warp & 3;
+    const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+    crs::publish<BT>(tbase, s_go[0] == 1, sSlots, ws_tile, rank, S, quad * 32 + lane, row);
   }
 
   tc_fence_before();
-  cluster_sync();
-
+  crs::sync_all();  // every partial of the cluster is in L2 / its owner's shared memory
+  tc_fence_after();
   if (warp >= 2) {
-    constexpr int NQ = CH / 4;
-    const int e = threadIdx.x - 64, ew = e >> 5, el = e & 31;
+    const int e = threadIdx.x - 64;
+    if (e == 0) crs::fetch<BT>(sSlots, ws_tile, rbar, rank, S);
     const int m0 = mt * BT;
-    const uint32_t my_part = smem_u32(sPart);
-#pragma unroll 1
-    for (int ci = rank; ci < BT / CH; ci += S) {
-      const int c = ci * CH;
-      float4 acc[NQ];
-#pragma unroll
-      for (int qq = 0; qq < NQ; ++qq) acc[qq] = make_float4(0.f, 0.f, 0.f, 0.f);
-      const uint32_t coff = (c * BW + e * 4) * 4;
-      for (uint32_t sp = 0; sp < S; ++sp) {
-        const uint32_t b = mapa(my_part, sp) + coff;
-        float4 x[NQ];
-#pragma unroll
-        for (int qq = 0; qq < NQ; ++qq) x[qq] = ld_dsmem4(b + qq * 128 * 16);
-#pragma unroll
-        for (int qq = 0; qq < NQ; ++qq) {
-          acc[qq].x += x[qq].x;
-          acc[qq].y += x[qq].y;
-          acc[qq].z += x[qq].z;
-          acc[qq].w += x[qq].w;
-        }
-      }
-#pragma unroll
-      for (int qq = 0; qq < NQ; ++qq) {
-        const int m = m0 + c + 4 * qq + ew;
-        const int r0 = 4 * el;
-        if (a.mode == 1) {
-          float4 up;
-          up.x = __shfl_down_sync(0xffffffffu, acc[qq].x, 16);
-          up.y = __shfl_down_sync(0xffffffffu, acc[qq].y, 16);
-          up.z = __shfl_down_sync(0xffffffffu, acc[qq].z, 16);
-          up.w = __shfl_down_sync(0xffffffffu, acc[qq].w, 16);
-          const int f = nt * 64 + r0;
-          if (el < 16 && m < a.M && f < (a.N >> 1)) {
-            uint2 pk;
-            pk.x = pack_bf16x2(silu_f(acc[qq].x) * up.x, silu_f(acc[qq].y) * up.y);
-            pk.y = pack_bf16x2(silu_f(acc[qq].z) * up.z, silu_f(acc[qq].w) * up.w);
-            *reinterpret_cast<uint2*>(reinterpret_cast<bf16*>(a.C) +
-                                      static_cast<size_t>(m) * a.ldc + f) = pk;
-          }
-        } else {
-          const int nn = nt * BW + r0;
-          if (m < a.M && nn < a.N) {
-            const float vv[4] = {acc[qq].x, acc[qq].y, acc[qq].z, acc[qq].w};
-            if (a.mode == 2) {
-              float* Cp = reinterpret_cast<float*>(a.C) + static_cast<size_t>(m) * a.ldc;
-              for (int u = 0; u < 4 && nn + u < a.N; ++u) Cp[nn + u] = vv[u];
-            } else {
-              bf16* Cp = reinterpret_cast<bf16*>(a.C) + static_cast<size_t>(m) * a.ldc;
-              if (nn + 3 < a.N && a.vec_ok) {
-                uint2 pk;
-                pk.x = pack_bf16x2(vv[0], vv[1]);
-                pk.y = pack_bf16x2(vv[2], vv[3]);
-                *reinterpret_cast<uint2*>(Cp + nn) = pk;
-              } else {
-                for (int u = 0; u < 4 && nn + u < a.N; ++u) Cp[nn + u] = __float2bfloat16(vv[u]);
-              }
-            }
-          }
-        }
-      }
+    auto epi = [&](int oc, int t0, int ew, int el, float4 (&acc)[4]) {
+      crs::stage_out(a.mode, sOut + oc * crs::OUT_BYTES, ew, el, acc, nullptr, 0, 0, 0);
+    };
+    const bool ok = crs::reduce<BT>(sSlots, rbar, rank, S, e, abort_flag, epi);
+    crs::store_out<BT>(&tmC, sOut, e, rank, S, a.mode == 1 ? nt * 64 : nt * BW, m0, false);
+    if (!ok) {
+      record_error(a.err, kErrTimeoutTmaFull);
+      *abort_flag = 1;
+      if (e == 0 && !mbar_wait(rbar, 0, nullptr, kWaitBudgetNs)) record_error(a.err, kErrTimeoutDrain);
     }
   }
-  cluster_sync();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -371,13 +311,14 @@ static PFN_cuTensorMapEncodeTiled_v12000 q_encode() {
   return fn;
 }
 
+bool make_tmap_out(const at::Tensor& C, int64_t mode, int M, int N, CUtensorMap* m);
 CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t inner, uint64_t outer,
                               uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
                               CUtensorMapSwizzle swz);
 
 template <int BT, int STAGES, int QBITS>
-static void launch_q(const CUtensorMap& tq, const CUtensorMap& tx, const q::Args& a, int S,
-                     cudaStream_t st) {
+static void launch_q(const CUtensorMap& tq, const CUtensorMap& tx, const CUtensorMap& tc,
+                     const q::Args& a, int S, cudaStream_t st) {
   using L = q::Smem<BT, STAGES, QBITS>;
   static bool attr = false;
   if (!attr) {
@@ -397,13 +338,13 @@ static void launch_q(const CUtensorMap& tq, const CUtensorMap& tx, const q::Args
   at[0].val.clusterDim.z = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, q::gemm_q_kernel<BT, STAGES, QBITS>, tq, tx, a));
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, q::gemm_q_kernel<BT, STAGES, QBITS>, tq, tx, tc, a));
 }
 
 // X [M, K] bf16; qw [N, K*bits/8] uint8; scales / offsets [N, K/group] fp16.
 void gemm_quant(const at::Tensor& X, const at::Tensor& qw, const at::Tensor& scales,
                 const at::Tensor& offsets, int64_t bits, int64_t group, at::Tensor& C,
-                int64_t mode, int64_t splits, at::Tensor& err) {
+                int64_t mode, int64_t splits, at::Tensor& err, at::Tensor& ws) {
   TORCH_CHECK(X.scalar_type() == at::kBFloat16 && X.stride(1) == 1, "gemm_quant: X bf16");
   TORCH_CHECK(qw.scalar_type() == at::kByte && qw.is_contiguous(), "gemm_quant: packed uint8");
   TORCH_CHECK(scales.scalar_type() == at::kHalf && offsets.scalar_type() == at::kHalf,
@@ -432,6 +373,13 @@ void gemm_quant(const at::Tensor& X, const at::Tensor& qw, const at::Tensor& sca
       if (tiles * s <= nsm && a.kb_total / s >= 2) S = s;
   }
   S = std::max(1, std::min(S, std::min(8, a.kb_total)));
+  {
+    const int stages = BT == 128 ? 5 : BT == 256 ? 4 : 6;
+    const int stage_bytes = 128 * 64 * 2 + 128 * 64 * static_cast<int>(bits) / 8 + BT * 64 * 2;
+    while (S > 1 && crs::smem_bytes(BT, S) > stages * stage_bytes) --S;
+    while (S > 1 && ws.numel() < crs::ws_floats(a.m_tiles * a.n_tiles, BT, S)) --S;
+  }
+  a.ws = S > 1 ? ws.data_ptr<float>() : nullptr;
   a.kb_per_split = (a.kb_total + S - 1) / S;
   a.scales = reinterpret_cast<const __half*>(scales.data_ptr());
   a.offsets = reinterpret_cast<const __half*>(offsets.data_ptr());
@@ -455,16 +403,19 @@ void gemm_quant(const at::Tensor& X, const at::Tensor& qw, const at::Tensor& sca
   }
   const CUtensorMap tx = make_tmap_bf16_2d(X.data_ptr(), K, M, X.stride(0) * 2, 64, BT,
                                            CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tc;
+  TORCH_CHECK(make_tmap_out(C, mode, M, N, &tc),
+              "gemm_quant: C must be 16-byte aligned with a 16-byte multiple row stride");
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
 #define LB_Q(BTV, STV)                                                    \
-  if (bits == 4) launch_q<BTV, STV, 4>(tq, tx, a, S, st);                 \
-  else launch_q<BTV, STV, 8>(tq, tx, a, S, st);
+  if (bits == 4) launch_q<BTV, STV, 4>(tq, tx, tc, a, S, st);             \
+  else launch_q<BTV, STV, 8>(tq, tx, tc, a, S, st);
   switch (BT) {
     case 16: LB_Q(16, 6) break;
     case 32: LB_Q(32, 6) break;
     case 64: LB_Q(64, 6) break;
-    case 128: LB_Q(128, 4) break;
-    default: LB_Q(256, 3) break;
+    case 128: LB_Q(128, 5) break;
+    default: LB_Q(256, 4) break;
   }
 #undef LB_Q
 }

@@ -27,6 +27,9 @@
 
 #include <mutex>
 
+#include <cstring>
+
+#include "cluster_rs.cuh"
 #include "common.cuh"
 
 namespace lb {
@@ -69,6 +72,7 @@ struct GemmArgs {
   unsigned long long* trace;  // optional: 8 globaltimer stamps per CTA (phase profiling)
   int vec_ok;                 // C base 16-byte aligned and ldc % 4 == 0: vector stores
   TpLink tp;
+  int tma_out;                // cluster kernel: output tiles through the tensor map tmC
 };
 
 __device__ __forceinline__ int ld_acquire_sys(const int* p) {
@@ -424,38 +428,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ======================================================================================
 // Cluster split-K variant for small token counts (decode).  The S CTAs of a thread-block
-// cluster own the same 128 x BT output tile and split K; each stages its fp32 partial in
-// its own shared memory (the drained pipeline buffers) and the tile is reduced through
-// distributed shared memory: CTA r sums every peer's partial for the 32-column chunks
-// c with c % S == r, in fixed rank order (deterministic), then runs the epilogue.  No
-// global workspace, no atomics.
+// cluster own the same 128 x BT output tile and split K; the fp32 accumulators are combined
+// by the push reduce-scatter of cluster_rs.cuh (16-column chunks, owner c % S, rank-order
+// sum: deterministic), and each owner runs the epilogue for its chunks.  No global
+// workspace, no atomics.
 // ======================================================================================
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t cluster_nctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
-}
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ float4 ld_dsmem_f32x4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr)
-               : "memory");
-  return v;
-}
 
 // Destination row of output token m: local C, or (tensor-parallel scatter) the owner rank's
 // reduce-scatter receive slot for this source rank, reached by P2P stores over NVLink.
@@ -471,34 +448,36 @@ __device__ __forceinline__ bf16* out_row(const GemmArgs& a, int m) {
 template <int BT, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_cluster_kernel(const __grid_constant__ CUtensorMap tmW,
-                           const __grid_constant__ CUtensorMap tmX, const GemmArgs a) {
+                           const __grid_constant__ CUtensorMap tmX,
+                           const __grid_constant__ CUtensorMap tmC, const GemmArgs a) {
   using L = GemmSmem<BT, STAGES>;
   constexpr int CH = L::CH;
   constexpr int TMEM_COLS = BT < 32 ? 32 : BT;
-  // Partial tile staged column-major ([token][weight row]); a CH-column chunk is one
-  // contiguous run of CH*128 floats that the owner CTA reduces as a flat array.
-  static_assert(BW * BT * 4 <= STAGES * (L::W_BYTES + L::X_BYTES), "partial must fit");
+  static_assert(crs::smem_bytes(BT, 2) <= STAGES * (L::W_BYTES + L::X_BYTES), "split-K slots");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sW = smem;
   uint8_t* sX = smem + STAGES * L::W_BYTES;
-  float* sPart = reinterpret_cast<float*>(smem);  // reused after the main loop: [BT][128]
-  float* sEpi = reinterpret_cast<float*>(sX + STAGES * L::X_BYTES);
+  // after the main loop: split-K slots, then the output staging tiles
+  float* sSlots = reinterpret_cast<float*>(smem);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* tfull = bars + 2 * STAGES;
   uint64_t* drain = tfull + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* rbar = drain + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* s_go = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const uint32_t S = cluster_nctarank();
-  const uint32_t rank = cluster_ctarank();
+  const uint32_t S = crs::nctarank();
+  const uint32_t rank = crs::ctarank();
+  uint8_t* sOut = smem + crs::num_slots(BT, S) * crs::SLOT_BYTES;
   const int tile = blockIdx.x / S;
+  float* ws_tile = a.ws + crs::ws_floats(tile, BT, S);
   const int mt = tile % a.m_tiles;
   const int nt = tile / a.m_tiles;
   const int kb0 = rank * a.kb_per_split;
@@ -513,6 +492,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(tfull, 1);
     mbar_init(drain, 1);
+    mbar_init(rbar, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -593,9 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) tc_commit(tfull);
     }
   } else {
-    // Epilogue warps: TMEM -> own shared-memory partial [BT][128] (column-major by token).
-    const int quad = warp & 3;
-    const int row = quad * 32 + lane;
+    // Epilogue warps: wait for the accumulator, publish the partial tile.
     const int etid = threadIdx.x - 64;
     if (etid == 0) {
       int go = 1;
@@ -610,118 +588,98 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (tr) tr[2] = globaltimer_ns();
     }
     named_bar_sync(1, 128);
-    const int go = s_go[0];
-    if (go == 1) {
-      tc_fence_after();
-      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
-#pragma unroll 1
-      for (int c = 0; c < BT; c += CH) {
-        uint32_t r[CH];
-        if constexpr (CH == 32) {
-          tmem_ld32(tbase + c, *reinterpret_cast<uint32_t(*)[32]>(r));
-        } else {
-          tmem_ld16(tbase + c, *reinterpret_cast<uint32_t(*)[16]>(r));
-        }
-        tc_wait_ld();
-#pragma unroll
-        for (int j = 0; j < CH; ++j) sPart[(c + j) * BW + row] = __uint_as_float(r[j]);
-      }
-    } else {
-      for (int c = 0; c < BT; ++c) sPart[c * BW + row] = 0.f;
-    }
+    tc_fence_after();
+    const int quad = warp & 3;
+    const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+    crs::publish<BT>(tbase, s_go[0] == 1, sSlots, ws_tile, rank, S, quad * 32 + lane, etid);
   }
 
-  // Every partial of the cluster is in shared memory after this barrier.
   tc_fence_before();
   if (tr && threadIdx.x == 64) tr[3] = globaltimer_ns();
-  cluster_sync_all();
+  crs::sync_all();  // every partial of the cluster is in L2 / its owner's shared memory
+  tc_fence_after();
   if (tr && threadIdx.x == 64) tr[4] = globaltimer_ns();
 
   if (warp >= 2) {
-    // Owner of chunk ci (ci % S == rank) reduces it as a flat [CH cols][128 rows] array:
-    // thread e reads float4 number e + 128 q (q < CH/4) from every peer, i.e. token column
-    // j = 4 q + (e >> 5) and weight rows 4 (e & 31) .. +3 -> coalesced 512-byte DSMEM
-    // loads per warp and 4 consecutive output features per lane.
-    constexpr int NQ = CH / 4;
     const int e = threadIdx.x - 64;
-    const int ew = e >> 5, el = e & 31;
+    if (e == 0) crs::fetch<BT>(sSlots, ws_tile, rbar, rank, S);
     const int m0 = mt * BT;
-    const uint32_t my_part = smem_u32(sPart);
-#pragma unroll 1
-    for (int ci = rank; ci < BT / CH; ci += S) {
-      const int c = ci * CH;
-      float4 acc[NQ];
-#pragma unroll
-      for (int q = 0; q < NQ; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-      const uint32_t coff = (c * BW + e * 4) * 4;
-      for (uint32_t sp = 0; sp < S; ++sp) {  // fixed rank order: deterministic
-        const uint32_t b = mapa_shared(my_part, sp) + coff;
-        float4 x[NQ];
-#pragma unroll
-        for (int q = 0; q < NQ; ++q) x[q] = ld_dsmem_f32x4(b + q * 128 * 16);
-#pragma unroll
-        for (int q = 0; q < NQ; ++q) {
-          acc[q].x += x[q].x;
-          acc[q].y += x[q].y;
-          acc[q].z += x[q].z;
-          acc[q].w += x[q].w;
-        }
+    const int omode = a.mode == kEpiSwiGLU ? crs::kOutSwiGLU
+                      : a.mode == kEpiF32  ? crs::kOutF32
+                                           : crs::kOutBf16;
+    // thread: weight rows 4 el .. +3, token columns t0 + ew + 4 q
+    auto epi = [&](int oc, int t0, int ew, int el, float4 (&acc)[4]) {
+      if (a.tma_out) {
+        const int mf = m0 + t0, n0 = nt * BW;
+        const bf16* res = a.residual != nullptr
+                              ? a.residual + static_cast<size_t>(mf) * a.ldr + n0
+                              : nullptr;
+        crs::stage_out(omode, sOut + oc * crs::OUT_BYTES, ew, el, acc, res, a.ldr, a.M - mf,
+                       a.N - n0);
+        return;
       }
+      // per-thread stores (tensor-parallel scatter into peers' slots, or unaligned C)
+      const int r0 = 4 * el;
 #pragma unroll
-      for (int q = 0; q < NQ; ++q) {
-        const int m = m0 + c + 4 * q + ew;
-        const int r0 = 4 * el;                 // first of 4 weight rows
+      for (int q = 0; q < 4; ++q) {
+        const int m = m0 + t0 + ew + 4 * q;
         if (a.mode == kEpiSwiGLU) {
-          // lanes 0..15 hold gate rows 0..63, lanes 16..31 the up rows of the same features
           float4 up;
           up.x = __shfl_down_sync(0xffffffffu, acc[q].x, 16);
           up.y = __shfl_down_sync(0xffffffffu, acc[q].y, 16);
           up.z = __shfl_down_sync(0xffffffffu, acc[q].z, 16);
           up.w = __shfl_down_sync(0xffffffffu, acc[q].w, 16);
           const int f = nt * 64 + r0;
-          if (el < 16 && m < a.M && f < (a.N >> 1) && a.vec_ok) {
-            bf16* C = out_row(a, m) + f;
+          if (el < 16 && m < a.M && f < (a.N >> 1)) {
             uint2 pk;
             pk.x = pack_bf16x2(silu(acc[q].x) * up.x, silu(acc[q].y) * up.y);
             pk.y = pack_bf16x2(silu(acc[q].z) * up.z, silu(acc[q].w) * up.w);
-            *reinterpret_cast<uint2*>(C) = pk;
+            *reinterpret_cast<uint2*>(out_row(a, m) + f) = pk;
           }
+          continue;
+        }
+        const int n = nt * BW + r0;
+        if (m >= a.M || n >= a.N) continue;
+        float vv[4] = {acc[q].x, acc[q].y, acc[q].z, acc[q].w};
+        if (a.mode == kEpiF32) {
+          float* C = reinterpret_cast<float*>(a.C) + static_cast<size_t>(m) * a.ldc;
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (n + u < a.N) C[n + u] = vv[u];
+          continue;
+        }
+        bf16* C = out_row(a, m);
+        if (a.residual != nullptr) {
+          const bf16* R = a.residual + static_cast<size_t>(m) * a.ldr;
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (n + u < a.N) vv[u] += __bfloat162float(R[n + u]);
+        }
+        if (n + 3 < a.N && a.vec_ok) {
+          uint2 pk;
+          pk.x = pack_bf16x2(vv[0], vv[1]);
+          pk.y = pack_bf16x2(vv[2], vv[3]);
+          *reinterpret_cast<uint2*>(C + n) = pk;
         } else {
-          const int n = nt * BW + r0;
-          if (m < a.M && n < a.N) {
-            float vv[4] = {acc[q].x, acc[q].y, acc[q].z, acc[q].w};
-            if (a.mode == kEpiF32) {
-              float* C = reinterpret_cast<float*>(a.C) + static_cast<size_t>(m) * a.ldc;
-              if (n + 3 < a.N && a.vec_ok) {
-                *reinterpret_cast<float4*>(C + n) = acc[q];
-              } else {
-                for (int u = 0; u < 4 && n + u < a.N; ++u) C[n + u] = vv[u];
-              }
-            } else {
-              bf16* C = out_row(a, m);
-              if (a.residual != nullptr) {
-                const bf16* R = a.residual + static_cast<size_t>(m) * a.ldr;
-                for (int u = 0; u < 4; ++u)
-                  if (n + u < a.N) vv[u] += __bfloat162float(R[n + u]);
-              }
-              if (n + 3 < a.N && a.vec_ok) {
-                uint2 pk;
-                pk.x = pack_bf16x2(vv[0], vv[1]);
-                pk.y = pack_bf16x2(vv[2], vv[3]);
-                *reinterpret_cast<uint2*>(C + n) = pk;
-              } else {
-                for (int u = 0; u < 4 && n + u < a.N; ++u) C[n + u] = __float2bfloat16(vv[u]);
-              }
-            }
-          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (n + u < a.N) C[n + u] = __float2bfloat16(vv[u]);
         }
       }
+    };
+    const bool ok = crs::reduce<BT>(sSlots, rbar, rank, S, e, abort_flag, epi);
+    if (a.tma_out)
+      crs::store_out<BT>(&tmC, sOut, e, rank, S, omode == crs::kOutSwiGLU ? nt * 64 : nt * BW,
+                         m0, a.tp.done_counter != nullptr);
+    if (!ok) {
+      record_error(a.err, kErrTimeoutTmaFull);
+      *abort_flag = 1;
+      // let the bulk copies of this CTA land before its shared memory is released
+      if (e == 0 && !mbar_wait(rbar, 0, nullptr, kWaitBudgetNs)) record_error(a.err, kErrTimeoutDrain);
     }
+    if (tr && e == 0) tr[5] = globaltimer_ns();
   }
-
-  // No CTA may leave while a peer still reads its shared memory.
-  if (tr && threadIdx.x == 64) tr[5] = globaltimer_ns();
-  cluster_sync_all();
+  __syncthreads();
   if (tr && threadIdx.x == 64) tr[6] = globaltimer_ns();
   if (a.tp.done_counter != nullptr && threadIdx.x == 0) {
     // Grid completion: the last CTA resets the consumed input flag and signals the owners.
@@ -791,6 +749,27 @@ CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t inner, uint64_t outer,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", static_cast<int>(r));
   return m;
+}
+
+// Tensor map of the output for the cluster kernel's TMA-store epilogue: boxes of 16 tokens x
+// 128 columns (64 for SwiGLU), no swizzle.  False when C's base or row stride is not 16-byte
+// aligned (the kernel then stores per thread).
+bool make_tmap_out(const at::Tensor& C, int64_t mode, int M, int N, CUtensorMap* m) {
+  const bool f32 = mode == kEpiF32;
+  const int esz = f32 ? 4 : 2;
+  const uint64_t cols = mode == kEpiSwiGLU ? N / 2 : N;
+  const uint64_t stride = static_cast<uint64_t>(C.stride(0)) * esz;
+  if (reinterpret_cast<uintptr_t>(C.data_ptr()) % 16 != 0 || stride % 16 != 0 || cols == 0)
+    return false;
+  cuuint64_t dims[2] = {cols, static_cast<cuuint64_t>(M)};
+  cuuint64_t strides[1] = {stride};
+  cuuint32_t box[2] = {mode == kEpiSwiGLU ? 64u : 128u, 16u};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = encode_fn()(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                           2, C.data_ptr(), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
 }
 
 static int num_sms() {
@@ -867,12 +846,18 @@ static int active_clusters_for(int BT, int S) {
 
 // Cluster split-K factor: the largest S <= 8 whose grid (tiles x S CTAs) is co-resident in
 // one wave, keeping >= 2 k-blocks per CTA.  0 = the tiles alone fill the GPU (no cluster).
+// Whether the split-K receive slots of a cluster of S fit in the drained pipeline buffers.
+static bool cluster_fits(int BT, int S) {
+  const int stages = BT <= 64 ? 8 : BT == 128 ? 6 : 4;
+  return crs::smem_bytes(BT, S) <= stages * (BW * BK * 2 + BT * BK * 2);
+}
+
 static int pick_cluster(int BT, int tiles, int kb_total) {
   if (tiles >= num_sms()) return 0;
   int best = 1;
   for (int S = 2; S <= 8; ++S) {
     if (kb_total / S < 2) break;
-    if (tiles <= active_clusters_for(BT, S)) best = S;
+    if (cluster_fits(BT, S) && tiles <= active_clusters_for(BT, S)) best = S;
   }
   return best;
 }
@@ -888,7 +873,8 @@ std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t bt, int6
   if (splits < 0 || (splits == 0 && pick_cluster(BT, tiles, kb_total) > 1)) {
     int S = splits < 0 ? static_cast<int>(-splits) : pick_cluster(BT, tiles, kb_total);
     S = std::max(1, std::min(S, std::min(8, kb_total)));
-    return {BT, -S, tiles, 0};
+    while (S > 1 && !cluster_fits(BT, S)) --S;
+    return {BT, -S, tiles, S > 1 ? crs::ws_floats(tiles, BT, S) : 0};
   }
   int sp = splits > 0 ? static_cast<int>(splits) : 1;
   sp = std::max(1, std::min(sp, kb_total));
@@ -899,7 +885,8 @@ std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t bt, int6
 }
 
 template <int BT, int STAGES>
-static void launch_cluster(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a,
+static void launch_cluster(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tc,
+                           const GemmArgs& a,
                            int S, cudaStream_t st) {
   using L = GemmSmem<BT, STAGES>;
   static bool attr_set = false;
@@ -920,7 +907,7 @@ static void launch_cluster(const CUtensorMap& tw, const CUtensorMap& tx, const G
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_tc_cluster_kernel<BT, STAGES>, tw, tx, a));
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_tc_cluster_kernel<BT, STAGES>, tw, tx, tc, a));
 }
 
 void gemm_bf16(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
@@ -950,6 +937,8 @@ void gemm_bf16(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
   int sp = plan[1];
   const int tiles = plan[2];
   if (sp > 1 && (ws.numel() < plan[3] || counters.numel() < tiles)) sp = 1;
+  TORCH_CHECK(sp > 0 || ws.numel() >= plan[3], "gemm: cluster split-K workspace too small (",
+              ws.numel(), " < ", plan[3], " floats)");
   const int kb_total = (K + BK - 1) / BK;
   const int S = sp < 0 ? -sp : 1;
   const int nsplit = sp < 0 ? S : sp;
@@ -974,15 +963,16 @@ void gemm_bf16(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
     a.residual = reinterpret_cast<const bf16*>(residual->data_ptr());
     a.ldr = residual->stride(0);
   }
-  a.ws = sp > 1 ? ws.data_ptr<float>() : nullptr;
+  a.ws = (sp > 1 || sp < -1) ? ws.data_ptr<float>() : nullptr;
   a.counters = sp > 1 ? counters.data_ptr<int>() : nullptr;
   a.mode = mode;
   a.err = err.data_ptr<int>();
   a.vec_ok = (reinterpret_cast<uintptr_t>(C.data_ptr()) % 16 == 0) && (C.stride(0) % 4 == 0);
   TORCH_CHECK(mode != kEpiSwiGLU || a.vec_ok, "swiglu gemm: C must be 16-byte aligned, ldc % 4 == 0");
   a.trace = nullptr;
-  if (trace.has_value() && trace->defined())
+  if (trace.has_value() && trace->defined()) {
     a.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
+  }
 
   const CUtensorMap tw = make_tmap_bf16_2d(W.data_ptr(), K, N, W.stride(0) * 2, BK, BW,
                                            CU_TENSOR_MAP_SWIZZLE_128B);
@@ -990,12 +980,15 @@ void gemm_bf16(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
                                            CU_TENSOR_MAP_SWIZZLE_128B);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   if (sp < 0) {
+    CUtensorMap tc;
+    std::memset(&tc, 0, sizeof(tc));
+    a.tma_out = make_tmap_out(C, mode, M, N, &tc) ? 1 : 0;
     switch (BT) {
-      case 16: launch_cluster<16, 8>(tw, tx, a, S, st); break;
-      case 32: launch_cluster<32, 8>(tw, tx, a, S, st); break;
-      case 64: launch_cluster<64, 8>(tw, tx, a, S, st); break;
-      case 128: launch_cluster<128, 6>(tw, tx, a, S, st); break;
-      case 256: launch_cluster<256, 4>(tw, tx, a, S, st); break;
+      case 16: launch_cluster<16, 8>(tw, tx, tc, a, S, st); break;
+      case 32: launch_cluster<32, 8>(tw, tx, tc, a, S, st); break;
+      case 64: launch_cluster<64, 8>(tw, tx, tc, a, S, st); break;
+      case 128: launch_cluster<128, 6>(tw, tx, tc, a, S, st); break;
+      case 256: launch_cluster<256, 4>(tw, tx, tc, a, S, st); break;
       default: TORCH_CHECK(false, "gemm: unsupported token tile ", BT);
     }
     return;
@@ -1022,7 +1015,8 @@ void gemm_bf16_tp(const at::Tensor& A, const at::Tensor& W, at::Tensor& C, int64
                   at::Tensor& err, int64_t splits, std::vector<int64_t> scatter_ptrs,
                   std::vector<int64_t> signal_ptrs, int64_t rows_per_rank, int64_t src_rank,
                   int64_t slot_stride, int64_t wait_flag_ptr, int64_t wait_count,
-                  int64_t done_counter_ptr, int64_t trace_ptr) {
+                  int64_t done_counter_ptr, int64_t trace_ptr,
+                  const c10::optional<at::Tensor>& ws) {
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && W.scalar_type() == at::kBFloat16, "bf16");
   TORCH_CHECK(A.stride(1) == 1 && W.stride(1) == 1 && C.stride(1) == 1, "inner stride 1");
   const int M = A.size(0), K = A.size(1), N = W.size(0);
@@ -1035,7 +1029,11 @@ void gemm_bf16_tp(const at::Tensor& A, const at::Tensor& W, at::Tensor& C, int64
   const int kb_total = (K + BK - 1) / BK;
   int S = splits > 0 ? static_cast<int>(splits) : pick_cluster(BT, m_tiles * n_tiles, kb_total);
   S = std::max(1, std::min(S, std::min(8, kb_total)));
+  while (S > 1 && !cluster_fits(BT, S)) --S;
+  const bool have_ws = ws.has_value() && ws->defined();
+  while (S > 1 && (!have_ws || ws->numel() < crs::ws_floats(m_tiles * n_tiles, BT, S))) --S;
   GemmArgs a = {};
+  a.ws = S > 1 ? ws->data_ptr<float>() : nullptr;
   a.M = M;
   a.N = N;
   a.K = K;
@@ -1070,13 +1068,17 @@ void gemm_bf16_tp(const at::Tensor& A, const at::Tensor& W, at::Tensor& C, int64
                                            CU_TENSOR_MAP_SWIZZLE_128B);
   const CUtensorMap tx = make_tmap_bf16_2d(A.data_ptr(), K, M, A.stride(0) * 2, BK, BT,
                                            CU_TENSOR_MAP_SWIZZLE_128B);
+  // Local output (consumer GEMM): TMA-store epilogue; scatter into peers: per-thread P2P stores.
+  CUtensorMap tc;
+  std::memset(&tc, 0, sizeof(tc));
+  a.tma_out = (a.tp.world == 0 && make_tmap_out(C, mode, M, N, &tc)) ? 1 : 0;
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   switch (BT) {
-    case 16: launch_cluster<16, 8>(tw, tx, a, S, st); break;
-    case 32: launch_cluster<32, 8>(tw, tx, a, S, st); break;
-    case 64: launch_cluster<64, 8>(tw, tx, a, S, st); break;
-    case 128: launch_cluster<128, 6>(tw, tx, a, S, st); break;
-    default: launch_cluster<256, 4>(tw, tx, a, S, st); break;
+    case 16: launch_cluster<16, 8>(tw, tx, tc, a, S, st); break;
+    case 32: launch_cluster<32, 8>(tw, tx, tc, a, S, st); break;
+    case 64: launch_cluster<64, 8>(tw, tx, tc, a, S, st); break;
+    case 128: launch_cluster<128, 6>(tw, tx, tc, a, S, st); break;
+    default: launch_cluster<256, 4>(tw, tx, tc, a, S, st); break;
   }
 }
 

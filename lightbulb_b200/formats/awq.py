@@ -96,14 +96,6 @@ def awq_pack_gemm(q: torch.Tensor, z: torch.Tensor, s: torch.Tensor):
     return qweight, pack_int32_nibbles(zz), s.t().contiguous().to(torch.float16)
 
 
-def device_layout(q: torch.Tensor, z: torch.Tensor, s: torch.Tensor, device="cpu"):
-    """(q [N, K] 0..15) -> packed bytes [N, K/2] (low nibble = even k) + fp16 scales/zeros."""
-    n, k = q.shape
-    qb = (q[:, 0::2] | (q[:, 1::2] << 4)).to(torch.uint8)
-    return (qb.contiguous().to(device), s.to(torch.float16).contiguous().to(device),
-            z.to(torch.float16).contiguous().to(device))
-
-
 def random_awq_linear(out_f: int, in_f: int, group: int, gen: torch.Generator,
                       scale_lo: float = 0.001, scale_hi: float = 0.02):
     """Random uint4 weights, fp16 scales ~U[lo, hi], zeros U{0..15}."""

@@ -1,8 +1,14 @@
 """Quantized linear weights in the layout of the dequant-fused tcgen05 GEMM.
 
-``QuantWeight`` holds packed integers ``qw`` [N, K*bits/8] (uint8; 4-bit: two K-consecutive
-values per byte, low nibble first; 8-bit: signed bytes) and per-group fp16 ``scales`` /
-``offsets`` [N, K/group], with ``w = q * scale - offset``.  Converters:
+``QuantWeight`` holds packed integers ``qw`` [N, K*bits/8] and per-group fp16 ``scales`` /
+``offsets`` [N, K/group], with ``w = q * scale - offset``.  Packing (chosen so the GPU kernel
+converts without int->float instructions):
+
+* 4-bit: each little-endian 32-bit word holds 8 K-consecutive values e0..e7 with
+  e(2i) in bits [4i, 4i+4) and e(2i+1) in bits [16+4i, 20+4i);
+* 8-bit: one byte per value, stored as q + 128 (q signed).
+
+Converters:
 
 * AWQ (q 0..15, zero z, scale s, group 128):     scale = s, offset = z * s
 * GGUF Q8_0 (int8 q, fp16 d per 32):              scale = d, offset = 0
@@ -57,10 +63,8 @@ class QuantWeight:
     def unpack(self) -> torch.Tensor:
         """Integer values [N, K] (int16)."""
         if self.bits == 4:
-            lo = (self.qw & 0xF).to(torch.int16)
-            hi = (self.qw >> 4).to(torch.int16)
-            return torch.stack([lo, hi], -1).reshape(self.qw.shape[0], -1)
-        return self.qw.view(torch.int8).to(torch.int16)
+            return unpack4(self.qw)
+        return self.qw.to(torch.int16) - 128
 
     def dequantize(self, dtype=torch.float32) -> torch.Tensor:
         q = self.unpack().float()
@@ -68,6 +72,29 @@ class QuantWeight:
         s = self.scales.float().repeat_interleave(self.group, 1)
         o = self.offsets.float().repeat_interleave(self.group, 1)
         return (q * s - o).to(dtype)
+
+
+def pack4(q: torch.Tensor) -> torch.Tensor:
+    """[N, K] values 0..15 -> [N, K/2] uint8 in the kernel's word layout."""
+    n, k = q.shape
+    e = q.to(torch.int64).view(n, k // 8, 8)
+    word = torch.zeros(n, k // 8, dtype=torch.int64)
+    for i in range(4):
+        word |= e[:, :, 2 * i] << (4 * i)
+        word |= e[:, :, 2 * i + 1] << (16 + 4 * i)
+    b = torch.stack([(word >> (8 * j)) & 0xFF for j in range(4)], -1)
+    return b.to(torch.uint8).reshape(n, k // 2).contiguous()
+
+
+def unpack4(qw: torch.Tensor) -> torch.Tensor:
+    n, kb = qw.shape
+    b = qw.to(torch.int64).view(n, kb // 4, 4)
+    word = b[..., 0] | (b[..., 1] << 8) | (b[..., 2] << 16) | (b[..., 3] << 24)
+    out = torch.empty(n, kb // 4, 8, dtype=torch.int16)
+    for i in range(4):
+        out[..., 2 * i] = ((word >> (4 * i)) & 0xF).to(torch.int16)
+        out[..., 2 * i + 1] = ((word >> (16 + 4 * i)) & 0xF).to(torch.int16)
+    return out.reshape(n, kb * 2)
 
 
 def cat_rows(ws) -> QuantWeight:
@@ -91,8 +118,7 @@ def interleave_rows(gate: QuantWeight, up: QuantWeight, group_rows: int = 64) ->
 
 def from_awq(q: torch.Tensor, z: torch.Tensor, s: torch.Tensor, group: int) -> QuantWeight:
     """q [N, K] 0..15, z [N, K/g] 0..15, s [N, K/g]."""
-    q = q.to(torch.uint8)
-    qw = (q[:, 0::2] | (q[:, 1::2] << 4)).contiguous()
+    qw = pack4(q)
     sf = s.float()
     return QuantWeight(qw, sf.to(torch.float16), (z.float() * sf).to(torch.float16), 4, group)
 
@@ -100,8 +126,8 @@ def from_awq(q: torch.Tensor, z: torch.Tensor, s: torch.Tensor, group: int) -> Q
 def from_q8_0(raw: np.ndarray, n: int, k: int) -> QuantWeight:
     blk = raw.reshape(n, k // 32, 34)
     d = blk[:, :, 0:2].copy().view(np.float16).reshape(n, k // 32)
-    qs = blk[:, :, 2:].reshape(n, k).copy()
-    return QuantWeight(torch.from_numpy(qs).view(torch.uint8).contiguous(),
+    qs = (blk[:, :, 2:].reshape(n, k).view(np.int8).astype(np.int16) + 128).astype(np.uint8)
+    return QuantWeight(torch.from_numpy(qs).contiguous(),
                        torch.from_numpy(d.astype(np.float16)),
                        torch.zeros(n, k // 32, dtype=torch.float16), 8, 32)
 
@@ -130,7 +156,7 @@ def from_q4_k(raw: np.ndarray, n: int, k: int) -> QuantWeight:
     hi = qs >> 4
     vals = np.stack([lo, hi], axis=3).reshape(n, nb, 8, 32)    # sub-block order
     vals = vals.reshape(n, k).astype(np.uint8)
-    qw = torch.from_numpy((vals[:, 0::2] | (vals[:, 1::2] << 4)).astype(np.uint8))
+    qw = pack4(torch.from_numpy(vals))
     scale = (d[:, :, None] * sc).reshape(n, nb * 8)
     off = (dmin[:, :, None] * mn).reshape(n, nb * 8)
     return QuantWeight(qw.contiguous(), torch.from_numpy(scale.astype(np.float16)),

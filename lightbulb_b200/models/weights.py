@@ -257,6 +257,7 @@ def random_packed_awq_model(cfg: ModelConfig, seed: int = 0, rank: int = 0, worl
     layers = []
 
     def qlin(n, k):
+        # random uint4 values: any byte pattern is a valid packing of 8 random nibbles
         qw = torch.randint(0, 256, (n, k // 2), generator=g, device=device, dtype=torch.int32)
         s = torch.empty(n, k // group, device=device).uniform_(0.001, 0.02, generator=g)
         z = torch.randint(0, 16, (n, k // group), generator=g, device=device).float()

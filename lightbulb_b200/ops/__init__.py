@@ -173,8 +173,9 @@ def gemm_quant(a: torch.Tensor, w, out: Optional[torch.Tensor] = None, mode: int
         else:
             out = torch.empty(m, n, dtype=torch.bfloat16, device=a.device)
     if a.is_cuda:
+        sc = scratch(a.device)
         _need_c().gemm_quant(a, w.qw, w.scales, w.offsets, w.bits, w.group, out, mode,
-                             max(0, splits), scratch(a.device).err)
+                             max(0, splits), sc.err, sc.gemm_ws)
         _launches[0] += 1
         return out
     return gemm(a, w.dequantize(torch.bfloat16), out, None, mode)

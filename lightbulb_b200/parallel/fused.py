@@ -81,6 +81,7 @@ class FusedTP:
         # shape/stride carrier for scatter GEMMs (row stride H; the data goes to peers)
         self._row_shape = torch.empty(1, hidden, dtype=torch.bfloat16, device=device)
         self.err = ops.scratch(device).err
+        self.ws = ops.scratch(device).gemm_ws  # cluster split-K exchange
 
     # ------------------------------------------------------------------------------
     def gemm_consume(self, a: torch.Tensor, w: torch.Tensor, mode: int = ops.EPI_STORE):
@@ -93,7 +94,7 @@ class FusedTP:
         else:
             out = torch.empty(m, n, dtype=torch.bfloat16, device=a.device)
         self.C.gemm_bf16_tp(a, w, out, mode, self.err, 0, [], [], 0, self.rank, 0,
-                            self.g_flag, self.world, self.done)
+                            self.g_flag, self.world, self.done, ws=self.ws)
         ops.launch_counter_add(1)
         return out
 
@@ -101,7 +102,8 @@ class FusedTP:
         """Row-parallel GEMM whose output rows go straight to their owners (P2P)."""
         assert w.shape[0] == self.H
         self.C.gemm_bf16_tp(a, w, self._row_shape, ops.EPI_STORE, self.err, 0, self.rs_peers,
-                            self.rs_flag_peers, R, self.rank, R * self.H, 0, 0, self.done)
+                            self.rs_flag_peers, R, self.rank, R * self.H, 0, 0, self.done,
+                            ws=self.ws)
         ops.launch_counter_add(1)
 
     def norm_gather(self, w: torch.Tensor, R: int, eps: float, x_in=None,

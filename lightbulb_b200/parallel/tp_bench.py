@@ -105,7 +105,7 @@ def main(argv=None) -> int:
     torch.cuda.synchronize()
     comm.barrier()
     F.C.gemm_bf16_tp(attn, Wo, F._row_shape, ops.EPI_STORE, F.err, 0, F.rs_peers,
-                     F.rs_flag_peers, R, rank, R * H, 0, 0, F.done, tr_g.data_ptr())
+                     F.rs_flag_peers, R, rank, R * H, 0, 0, F.done, tr_g.data_ptr(), ws=F.ws)
     F.C.rs_norm_ag(F.rs_peers[rank], None, F.residual[:R], lnw, F.g_peers, F.g_flag_peers,
                    F.rs_flag, F.done, rank, R, R, 1e-5, True, F.err, tr_n.data_ptr())
     F.gemm_consume(F.gather[:T], Wgu, mode=ops.EPI_SWIGLU)

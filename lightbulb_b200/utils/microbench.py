@@ -43,6 +43,34 @@ def time_fn(fn, iters=20, warmup=3):
     return s.elapsed_time(e) / iters * 1e3  # us
 
 
+def time_graph(fn, calls: int, replays: int = 10) -> float:
+    """Device time per call with host launch cost removed: ``calls`` invocations of ``fn``
+    (each may use different, L2-busting operands) captured in one CUDA graph, replayed
+    between CUDA events."""
+    for _ in range(3):
+        fn()
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        fn()
+    torch.cuda.current_stream().wait_stream(st)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(calls):
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(replays):
+        g.replay()
+    e.record()
+    torch.cuda.synchronize()
+    del g
+    return s.elapsed_time(e) / (calls * replays) * 1e3
+
+
 def bench_gemm(m, n, k, copies=None, mode=ops.EPI_STORE, bt=0, splits=0, iters=20):
     bw, fl, src = peaks()
     wbytes = n * k * 2
@@ -55,14 +83,14 @@ def bench_gemm(m, n, k, copies=None, mode=ops.EPI_STORE, bt=0, splits=0, iters=2
         ops.gemm(a, ws[it[0] % copies], mode=mode, bt=bt, splits=splits)
         it[0] += 1
 
-    us = time_fn(run, iters=iters * copies if copies < 8 else iters)
+    us = time_graph(run, calls=max(copies, iters))
     it[0] = 0
 
     def run_cublas():
         torch.matmul(a, ws[it[0] % copies].T)
         it[0] += 1
 
-    us_cublas = time_fn(run_cublas, iters=iters * copies if copies < 8 else iters)
+    us_cublas = time_graph(run_cublas, calls=max(copies, iters))
     flops = 2 * m * n * k
     byts = wbytes + m * k * 2 + m * n * (4 if mode == ops.EPI_F32 else 2)
     t_roof = max(flops / fl, byts / bw) * 1e6
@@ -73,6 +101,33 @@ def bench_gemm(m, n, k, copies=None, mode=ops.EPI_STORE, bt=0, splits=0, iters=2
             "plan_bt_splits": plan[:2], "cublas_us": round(us_cublas, 2)}
 
 
+def bench_gemm_quant(m, n, k, kind="awq", iters=20):
+    """Dequant-fused GEMM on random quantized weights (> L2 of distinct copies)."""
+    from ..formats.quant import QuantWeight
+    bw, fl, src = peaks()
+    bits, group = (8, 32) if kind == "q80" else (4, 128 if kind == "awq" else 32)
+    wbytes = n * k * bits // 8 + 2 * 2 * n * (k // group)
+    copies = max(1, math.ceil(512e6 / wbytes))
+    ws = []
+    for _ in range(copies):
+        qw = torch.randint(0, 256, (n, k * bits // 8), device="cuda", dtype=torch.int32)
+        sc = torch.rand(n, k // group, device="cuda").half() * 0.01
+        ws.append(QuantWeight(qw.to(torch.uint8), sc, sc * 8, bits, group))
+    a = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+    it = [0]
+
+    def run():
+        ops.gemm(a, ws[it[0] % copies])
+        it[0] += 1
+
+    us = time_graph(run, calls=max(copies, iters))
+    byts = wbytes + m * k * 2 + m * n * 2
+    t_roof = max(2 * m * n * k / fl, byts / bw) * 1e6
+    return {"op": f"gemm_{kind}", "m": m, "n": n, "k": k, "us": round(us, 2),
+            "weight_bytes": wbytes, "gbs": round(byts / us / 1e3, 1),
+            "roofline_us": round(t_roof, 2), "frac_of_" + src: round(t_roof / us, 3)}
+
+
 def trace_gemm(m, n, k, bt=0, splits=0):
     """Per-CTA phase times (us) of one cluster split-K GEMM launch (globaltimer stamps)."""
     from .. import _C
@@ -81,15 +136,22 @@ def trace_gemm(m, n, k, bt=0, splits=0):
     out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
     s = ops.scratch(a.device)
     tr = torch.zeros(4096 * 8, dtype=torch.int64, device="cuda")
+    # warm the clocks first (a second of dense GEMMs), then three traced launches
+    x = torch.randn(8192, 8192, device="cuda", dtype=torch.bfloat16)
+    t_end = __import__("time").time() + 1.0
+    while __import__("time").time() < t_end:
+        x @ x
     for _ in range(3):
         _C.gemm_bf16(a, w, out, None, 0, s.gemm_ws, s.gemm_counters, s.err, bt, splits, tr)
     torch.cuda.synchronize()
-    t = tr.view(-1, 8).cpu()
-    t = t[t[:, 0] > 0].double()
+    plan = ops.gemm_plan(m, n, k, bt, splits)
+    grid = plan[2] * abs(plan[1])
+    t_all = tr.view(-1, 8).cpu()
+    t = t_all[:grid].double()
     t0 = t[:, 0].min()
-    names = ["start", "prologue", "acc_ready", "partial_staged", "cluster_sync1", "reduced",
-             "cluster_sync2"]
-    res = {"op": "gemm_trace", "m": m, "n": n, "k": k, "ctas": int(t.shape[0])}
+    names = ["start", "prologue", "acc_ready", "published", "synced", "reduced_stored",
+             "exit"]
+    res = {"op": "gemm_trace", "m": m, "n": n, "k": k, "ctas": grid}
     for i, nm in enumerate(names):
         col = t[:, i]
         ok = col > 0
@@ -116,7 +178,7 @@ def bench_decode_attn(batch, ctx, hq, hkv, bs=16, splits=None, iters=20):
     def run():
         ops.paged_attention(q, kc, vc, bt, sl, cu, out, hq // hkv, decode=True, num_splits=sp)
 
-    us = time_fn(run, iters=iters)
+    us = time_graph(run, calls=iters)
     byts = batch * ctx * hkv * d * 2 * 2
     return {"op": "attn_decode", "batch": batch, "ctx": ctx, "hq": hq, "hkv": hkv, "splits": sp,
             "us": round(us, 2), "gbs": round(byts / us / 1e3, 1),
@@ -139,20 +201,20 @@ def bench_decode(batch, ctx, tp=1, model="llama3-8b"):
     x = torch.randn(batch, h, device="cuda").to(torch.bfloat16)
     r = torch.randn(batch, h, device="cuda").to(torch.bfloat16)
     w = torch.ones(h, device="cuda", dtype=torch.bfloat16)
-    rows.append({"op": "rmsnorm_add", "us": round(time_fn(lambda: ops.rmsnorm(x, w, 1e-5, residual=r)), 2)})
+    rows.append({"op": "rmsnorm_add", "us": round(time_graph(lambda: ops.rmsnorm(x, w, 1e-5, residual=r), 20), 2)})
     qkv = torch.randn(batch, (hq + 2 * hkv) * d, device="cuda").to(torch.bfloat16)
     pos = torch.arange(batch, dtype=torch.int32, device="cuda")
     slots = torch.arange(batch, dtype=torch.int32, device="cuda")
     cs = ops.rope_table(4096, d, cfg.rope_theta, "cuda")
     kc = torch.zeros(batch, hkv, 16, d, device="cuda", dtype=torch.bfloat16)
-    rows.append({"op": "rope_kv", "us": round(time_fn(
-        lambda: ops.rope_kv(qkv, pos, slots, cs, kc, kc, hq, hkv)), 2)})
+    rows.append({"op": "rope_kv", "us": round(time_graph(
+        lambda: ops.rope_kv(qkv, pos, slots, cs, kc, kc, hq, hkv), 20), 2)})
     logits = torch.randn(batch, cfg.vocab_size, device="cuda")
     z = torch.zeros(batch, device="cuda")
     zi = torch.zeros(batch, dtype=torch.int32, device="cuda")
     seeds = torch.zeros(batch, dtype=torch.int64, device="cuda")
-    rows.append({"op": "sample_greedy", "us": round(time_fn(
-        lambda: ops.sample(logits, z, zi, z + 1, seeds)), 2)})
+    rows.append({"op": "sample_greedy", "us": round(time_graph(
+        lambda: ops.sample(logits, z, zi, z + 1, seeds), 20), 2)})
     per_layer = sum(r["us"] for r in rows[:4]) + rows[5]["us"] + 2 * rows[6]["us"] + rows[7]["us"]
     total = cfg.num_layers * per_layer + rows[4]["us"] + rows[8]["us"]
     rows.append({"op": "estimated_step_us", "us": round(total, 1),
@@ -162,7 +224,8 @@ def bench_decode(batch, ctx, tp=1, model="llama3-8b"):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["decode", "gemm", "attn", "gemm_trace"])
+    ap.add_argument("what", choices=["decode", "gemm", "attn", "gemm_trace", "gemm_quant"])
+    ap.add_argument("--kind", default="awq", choices=["awq", "q4k", "q80"])
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--ctx", type=int, default=1200)
     ap.add_argument("--tp", type=int, default=1)
@@ -178,6 +241,8 @@ def main(argv=None):
     torch.cuda.set_device(0)
     if a.what == "decode":
         rows = bench_decode(a.batch, a.ctx, a.tp, a.model)
+    elif a.what == "gemm_quant":
+        rows = [bench_gemm_quant(a.m, a.n, a.k, a.kind)]
     elif a.what == "gemm_trace":
         rows = [trace_gemm(a.m, a.n, a.k, a.bt, a.splits)]
     elif a.what == "gemm":

@@ -218,11 +218,12 @@ def test_sampling_distribution():
     assert torch.allclose(counts[:4] / 400, p, atol=0.08)
 
 
-@pytest.mark.parametrize("S", [1, 2, 3, 4, 8])
-@pytest.mark.parametrize("m,bt", [(5, 16), (64, 64), (256, 256), (130, 128)])
-def test_gemm_cluster_splitk(S, m, bt):
+@pytest.mark.parametrize("S", [1, 2, 3, 4, 6, 8])
+@pytest.mark.parametrize("m,bt,n", [(5, 16, 640), (64, 64, 600), (256, 256, 640), (130, 128, 700),
+                                    (33, 32, 256)])
+def test_gemm_cluster_splitk(S, m, bt, n):
     torch.manual_seed(S * 100 + m)
-    n, k = 640, 2048
+    k = 2048
     a = torch.randn(m, k, device=DEV).to(torch.bfloat16)
     w = (torch.randn(n, k, device=DEV) * 0.05).to(torch.bfloat16)
     r = torch.randn(m, n, device=DEV).to(torch.bfloat16)

@@ -57,10 +57,12 @@ def test_gemm_quant_gpu(kind, m):
     out = ops.gemm(a.cuda(), wd)
     torch.cuda.synchronize()
     ops.check_errors()
-    assert _rel(out.cpu(), ref) < 1.5e-2
-    for sp in (1, 3):
+    # exact dequantisation, bf16 operand and output rounding only (~1.5e-3)
+    assert _rel(out.cpu(), ref) < 5e-3
+    for sp in (1, 2, 3, 4, 8):
         o2 = ops.gemm_quant(a.cuda(), wd, splits=sp)
-        assert _rel(o2.cpu(), ref) < 1.5e-2
+        ops.check_errors()
+        assert _rel(o2.cpu(), ref) < 5e-3, sp
 
 
 @pytest.mark.gpu
@@ -74,4 +76,4 @@ def test_gemm_quant_swiglu_gpu():
     a = (torch.randn(40, k) * 0.1).to(torch.bfloat16)
     ref = torch.nn.functional.silu(a.float() @ gq.dequantize().T) * (a.float() @ uq.dequantize().T)
     out = ops.gemm(a.cuda(), w.to("cuda"), mode=ops.EPI_SWIGLU)
-    assert _rel(out.cpu(), ref) < 2e-2
+    assert _rel(out.cpu(), ref) < 1e-2
