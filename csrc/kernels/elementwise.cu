@@ -95,21 +95,23 @@ __global__ void rmsnorm_kernel(const bf16* x, int ldx, bf16* residual, int ldr, 
 }
 
 // ---------------------------------------------------------------------------------------
-// RoPE + KV append.  qkv: [T, (Hq + 2 Hkv) * D] (q rotated in place).  cos_sin: [P, D]
-// fp32 (first D/2 = cos, next D/2 = sin).  slot[t] = block * BS + offset (int32, < 0: skip).
-// Cache: [num_blocks, Hkv, BS, D].
+// RoPE + KV append.  qkv: [T, (Hq + 2 Hkv) * D] (q rotated in place).  cos_sin: [P, R]
+// fp32 (first R/2 = cos, next R/2 = sin), R <= D the rotary width (the true head_dim when
+// heads are zero-padded to D; lanes >= R are copied unrotated).  slot[t] = block * BS +
+// offset (int32, < 0: skip).  Cache: [num_blocks, Hkv, BS, D].
 // ---------------------------------------------------------------------------------------
 __global__ void rope_kv_kernel(bf16* qkv, int ld, const int* positions, const int* slots,
                                const float* cos_sin, int max_pos, bf16* k_cache, bf16* v_cache,
-                               int hq, int hkv, int head_dim, int block_size, int* err) {
+                               int hq, int hkv, int head_dim, int rot_dim, int block_size,
+                               int* err) {
   const int t = blockIdx.x;
   int pos = positions[t];
   if (pos < 0 || pos >= max_pos) {
     if (threadIdx.x == 0) record_error(err, kErrBounds);
     pos = 0;
   }
-  const int half = head_dim / 2;
-  const float* cs = cos_sin + static_cast<size_t>(pos) * head_dim;
+  const int half = rot_dim / 2;
+  const float* cs = cos_sin + static_cast<size_t>(pos) * rot_dim;
   bf16* row = qkv + static_cast<size_t>(t) * ld;
   const int64_t slot = slots != nullptr ? static_cast<int64_t>(slots[t]) : -1;
   const int64_t blk = slot >= 0 ? slot / block_size : 0;
@@ -132,6 +134,15 @@ __global__ void rope_kv_kernel(bf16* qkv, int ld, const int* positions, const in
       bf16* dst = k_cache + ((blk * hkv + kh) * block_size + off) * head_dim;
       dst[i] = r1;
       dst[i + half] = r2;
+    }
+  }
+  // k lanes beyond the rotary width (zero padding) are copied as they are
+  if (slot >= 0 && rot_dim < head_dim) {
+    const int extra = head_dim - rot_dim;
+    for (int idx = threadIdx.x; idx < hkv * extra; idx += blockDim.x) {
+      const int kh = idx / extra, dd = rot_dim + idx % extra;
+      k_cache[((blk * hkv + kh) * block_size + off) * head_dim + dd] =
+          row[(hq + kh) * head_dim + dd];
     }
   }
   if (slot >= 0) {
@@ -193,7 +204,9 @@ void rope_kv(at::Tensor& qkv, const at::Tensor& positions, const c10::optional<a
              int64_t hkv, at::Tensor& err) {
   const int T = qkv.size(0);
   if (T == 0) return;
-  const int D = cos_sin.size(1);
+  const int D = k_cache.size(3);      // head width (padded)
+  const int R = cos_sin.size(1);      // rotary width
+  TORCH_CHECK(R <= D && R % 2 == 0 && D % 8 == 0, "rope_kv: rotary width");
   TORCH_CHECK(qkv.stride(1) == 1 && qkv.size(1) >= (hq + 2 * hkv) * D, "rope_kv: qkv layout");
   TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous(), "cos_sin f32");
   const int* sp = nullptr;
@@ -201,7 +214,7 @@ void rope_kv(at::Tensor& qkv, const at::Tensor& positions, const c10::optional<a
   rope_kv_kernel<<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<bf16*>(qkv.data_ptr()), qkv.stride(0), positions.data_ptr<int>(), sp,
       cos_sin.data_ptr<float>(), cos_sin.size(0), reinterpret_cast<bf16*>(k_cache.data_ptr()),
-      reinterpret_cast<bf16*>(v_cache.data_ptr()), hq, hkv, D, k_cache.size(2),
+      reinterpret_cast<bf16*>(v_cache.data_ptr()), hq, hkv, D, R, k_cache.size(2),
       err.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

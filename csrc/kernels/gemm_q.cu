@@ -64,7 +64,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   using L = Smem<BT, STAGES, QBITS>;
   constexpr int CH = L::CH;
   constexpr int TMEM_COLS = BT < 32 ? 32 : BT;
-  static_assert(crs::smem_bytes(BT, 2) <= STAGES * L::STAGE, "split-K slots");
+  static_assert(crs::smem_bytes(BT, 1) <= STAGES * L::STAGE &&
+                    crs::smem_bytes(BT, 8) <= STAGES * L::STAGE,
+                "split-K slots");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -85,7 +87,6 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t S = crs::nctarank(), rank = crs::ctarank();
-  uint8_t* sOut = smem + crs::num_slots(BT, S) * crs::SLOT_BYTES;  // output staging
   const int tile = blockIdx.x / S;
   const int mt = tile % a.m_tiles, nt = tile / a.m_tiles;
   float* ws_tile = a.ws + crs::ws_floats(tile, BT, S);
@@ -279,10 +280,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (e == 0) crs::fetch<BT>(sSlots, ws_tile, rbar, rank, S);
     const int m0 = mt * BT;
     auto epi = [&](int oc, int t0, int ew, int el, float4 (&acc)[4]) {
-      crs::stage_out(a.mode, sOut + oc * crs::OUT_BYTES, ew, el, acc, nullptr, 0, 0, 0);
+      crs::stage_out(a.mode, crs::out_tile(sSlots, a.mode, oc), ew, el, acc, nullptr, 0, 0, 0);
     };
     const bool ok = crs::reduce<BT>(sSlots, rbar, rank, S, e, abort_flag, epi);
-    crs::store_out<BT>(&tmC, sOut, e, rank, S, a.mode == 1 ? nt * 64 : nt * BW, m0, false);
+    crs::store_out<BT>(&tmC, sSlots, a.mode, e, rank, S, a.mode == 1 ? nt * 64 : nt * BW, m0,
+                       false);
     if (!ok) {
       record_error(a.err, kErrTimeoutTmaFull);
       *abort_flag = 1;
@@ -311,7 +313,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 q_encode() {
   return fn;
 }
 
-bool make_tmap_out(const at::Tensor& C, int64_t mode, int M, int N, CUtensorMap* m);
+bool make_tmap_out(const at::Tensor& C, int64_t mode, int M, int N, int box_rows, CUtensorMap* m);
 CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t inner, uint64_t outer,
                               uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
                               CUtensorMapSwizzle swz);
@@ -320,6 +322,8 @@ template <int BT, int STAGES, int QBITS>
 static void launch_q(const CUtensorMap& tq, const CUtensorMap& tx, const CUtensorMap& tc,
                      const q::Args& a, int S, cudaStream_t st) {
   using L = q::Smem<BT, STAGES, QBITS>;
+  TORCH_CHECK(crs::smem_bytes(BT, S) <= STAGES * L::STAGE,
+              "gemm_quant: split-K slots exceed the pipeline buffers (BT ", BT, ", S ", S, ")");
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(q::gemm_q_kernel<BT, STAGES, QBITS>,
@@ -404,7 +408,7 @@ void gemm_quant(const at::Tensor& X, const at::Tensor& qw, const at::Tensor& sca
   const CUtensorMap tx = make_tmap_bf16_2d(X.data_ptr(), K, M, X.stride(0) * 2, 64, BT,
                                            CU_TENSOR_MAP_SWIZZLE_128B);
   CUtensorMap tc;
-  TORCH_CHECK(make_tmap_out(C, mode, M, N, &tc),
+  TORCH_CHECK(make_tmap_out(C, mode, M, N, crs::out_box_rows(BT, S), &tc),
               "gemm_quant: C must be 16-byte aligned with a 16-byte multiple row stride");
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
 #define LB_Q(BTV, STV)                                                    \

@@ -453,7 +453,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   using L = GemmSmem<BT, STAGES>;
   constexpr int CH = L::CH;
   constexpr int TMEM_COLS = BT < 32 ? 32 : BT;
-  static_assert(crs::smem_bytes(BT, 2) <= STAGES * (L::W_BYTES + L::X_BYTES), "split-K slots");
+  static_assert(crs::smem_bytes(BT, 1) <= STAGES * (L::W_BYTES + L::X_BYTES) &&
+                    crs::smem_bytes(BT, 8) <= STAGES * (L::W_BYTES + L::X_BYTES),
+                "split-K slots");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -475,7 +477,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   const uint32_t S = crs::nctarank();
   const uint32_t rank = crs::ctarank();
-  uint8_t* sOut = smem + crs::num_slots(BT, S) * crs::SLOT_BYTES;
   const int tile = blockIdx.x / S;
   float* ws_tile = a.ws + crs::ws_floats(tile, BT, S);
   const int mt = tile % a.m_tiles;
@@ -591,7 +592,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const int quad = warp & 3;
     const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
-    crs::publish<BT>(tbase, s_go[0] == 1, sSlots, ws_tile, rank, S, quad * 32 + lane, etid);
+    unsigned long long* tr2 = tr ? a.trace + (gridDim.x + blockIdx.x) * 8 : nullptr;
+    crs::publish<BT>(tbase, s_go[0] == 1, sSlots, ws_tile, rank, S, quad * 32 + lane, etid, tr2);
   }
 
   tc_fence_before();
@@ -614,8 +616,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bf16* res = a.residual != nullptr
                               ? a.residual + static_cast<size_t>(mf) * a.ldr + n0
                               : nullptr;
-        crs::stage_out(omode, sOut + oc * crs::OUT_BYTES, ew, el, acc, res, a.ldr, a.M - mf,
-                       a.N - n0);
+        crs::stage_out(omode, crs::out_tile(sSlots, omode, oc), ew, el, acc, res, a.ldr,
+                       a.M - mf, a.N - n0);
         return;
       }
       // per-thread stores (tensor-parallel scatter into peers' slots, or unaligned C)
@@ -667,10 +669,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     };
-    const bool ok = crs::reduce<BT>(sSlots, rbar, rank, S, e, abort_flag, epi);
+    unsigned long long* tr2 = tr ? a.trace + (gridDim.x + blockIdx.x) * 8 : nullptr;
+    const bool ok = crs::reduce<BT>(sSlots, rbar, rank, S, e, abort_flag, epi, tr2);
     if (a.tma_out)
-      crs::store_out<BT>(&tmC, sOut, e, rank, S, omode == crs::kOutSwiGLU ? nt * 64 : nt * BW,
-                         m0, a.tp.done_counter != nullptr);
+      crs::store_out<BT>(&tmC, sSlots, omode, e, rank, S, omode == crs::kOutSwiGLU ? nt * 64 : nt * BW,
+                         m0, a.tp.done_counter != nullptr, tr2);
     if (!ok) {
       record_error(a.err, kErrTimeoutTmaFull);
       *abort_flag = 1;
@@ -751,10 +754,10 @@ CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t inner, uint64_t outer,
   return m;
 }
 
-// Tensor map of the output for the cluster kernel's TMA-store epilogue: boxes of 16 tokens x
-// 128 columns (64 for SwiGLU), no swizzle.  False when C's base or row stride is not 16-byte
+// Tensor map of the output for the cluster kernel's TMA-store epilogue: boxes of box_rows tokens
+// x 128 columns (64 for SwiGLU), no swizzle.  False when C's base or row stride is not 16-byte
 // aligned (the kernel then stores per thread).
-bool make_tmap_out(const at::Tensor& C, int64_t mode, int M, int N, CUtensorMap* m) {
+bool make_tmap_out(const at::Tensor& C, int64_t mode, int M, int N, int box_rows, CUtensorMap* m) {
   const bool f32 = mode == kEpiF32;
   const int esz = f32 ? 4 : 2;
   const uint64_t cols = mode == kEpiSwiGLU ? N / 2 : N;
@@ -763,7 +766,7 @@ bool make_tmap_out(const at::Tensor& C, int64_t mode, int M, int N, CUtensorMap*
     return false;
   cuuint64_t dims[2] = {cols, static_cast<cuuint64_t>(M)};
   cuuint64_t strides[1] = {stride};
-  cuuint32_t box[2] = {mode == kEpiSwiGLU ? 64u : 128u, 16u};
+  cuuint32_t box[2] = {mode == kEpiSwiGLU ? 64u : 128u, static_cast<cuuint32_t>(box_rows)};
   cuuint32_t es[2] = {1, 1};
   CUresult r = encode_fn()(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                            2, C.data_ptr(), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -889,6 +892,8 @@ static void launch_cluster(const CUtensorMap& tw, const CUtensorMap& tx, const C
                            const GemmArgs& a,
                            int S, cudaStream_t st) {
   using L = GemmSmem<BT, STAGES>;
+  TORCH_CHECK(crs::smem_bytes(BT, S) <= STAGES * (L::W_BYTES + L::X_BYTES),
+              "gemm: split-K slots exceed the pipeline buffers (BT ", BT, ", S ", S, ")");
   static bool attr_set = false;
   if (!attr_set) {
     cudaFuncSetAttribute(gemm_tc_cluster_kernel<BT, STAGES>,
@@ -982,7 +987,7 @@ void gemm_bf16(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
   if (sp < 0) {
     CUtensorMap tc;
     std::memset(&tc, 0, sizeof(tc));
-    a.tma_out = make_tmap_out(C, mode, M, N, &tc) ? 1 : 0;
+    a.tma_out = make_tmap_out(C, mode, M, N, crs::out_box_rows(BT, S), &tc) ? 1 : 0;
     switch (BT) {
       case 16: launch_cluster<16, 8>(tw, tx, tc, a, S, st); break;
       case 32: launch_cluster<32, 8>(tw, tx, tc, a, S, st); break;
@@ -1071,7 +1076,8 @@ void gemm_bf16_tp(const at::Tensor& A, const at::Tensor& W, at::Tensor& C, int64
   // Local output (consumer GEMM): TMA-store epilogue; scatter into peers: per-thread P2P stores.
   CUtensorMap tc;
   std::memset(&tc, 0, sizeof(tc));
-  a.tma_out = (a.tp.world == 0 && make_tmap_out(C, mode, M, N, &tc)) ? 1 : 0;
+  a.tma_out =
+      (a.tp.world == 0 && make_tmap_out(C, mode, M, N, crs::out_box_rows(BT, S), &tc)) ? 1 : 0;
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   switch (BT) {
     case 16: launch_cluster<16, 8>(tw, tx, tc, a, S, st); break;

@@ -105,7 +105,7 @@ __global__ void kv_compact_kernel(bf16* storage, const int* src, const int* dst,
 }
 
 void h2o_accumulate(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& block_tables,
-                    const at::Tensor& seq_lens, at::Tensor& score, double decay) {
+                    const at::Tensor& seq_lens, at::Tensor& score, double decay, double scale) {
   const int B = seq_lens.size(0);
   if (B == 0) return;
   TORCH_CHECK(q.size(-1) == HD && k_cache.size(3) == HD, "h2o: head dim 128");
@@ -113,8 +113,7 @@ void h2o_accumulate(const at::Tensor& q, const at::Tensor& k_cache, const at::Te
       reinterpret_cast<const bf16*>(q.data_ptr()), q.stride(0),
       reinterpret_cast<const bf16*>(k_cache.data_ptr()), block_tables.data_ptr<int>(),
       block_tables.stride(0), seq_lens.data_ptr<int>(), score.data_ptr<float>(), q.size(1),
-      k_cache.size(1), k_cache.size(2), static_cast<float>(1.0 / std::sqrt(128.0)),
-      static_cast<float>(decay));
+      k_cache.size(1), k_cache.size(2), static_cast<float>(scale), static_cast<float>(decay));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

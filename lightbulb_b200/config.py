@@ -44,6 +44,15 @@ class ModelConfig:
         return self.num_heads * self.head_dim
 
     @property
+    def head_dim_padded(self) -> int:
+        """Head width of the device layout.  The attention kernels are built for 128-wide heads;
+        narrower heads (TinyLlama / Llama-3.2-1B 64, Phi-3 96) are zero-padded to 128: the
+        padded q / k / v lanes stay exactly zero, so scores and outputs are unchanged."""
+        if self.head_dim > 128 or self.head_dim % 16:
+            raise ValueError(f"head_dim {self.head_dim}: supported are multiples of 16 up to 128")
+        return 128
+
+    @property
     def kv_size(self) -> int:
         return self.num_kv_heads * self.head_dim
 

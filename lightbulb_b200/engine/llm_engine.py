@@ -64,7 +64,8 @@ def derive_num_blocks(cfg: ModelConfig, cache: CacheConfig, tp_size: int, device
     if cache.num_blocks > 0:
         return cache.num_blocks
     hkv = max(1, cfg.num_kv_heads // tp_size)
-    per_block = KVCache.bytes_per_block(cfg.num_layers, hkv, cache.block_size, cfg.head_dim)
+    per_block = KVCache.bytes_per_block(cfg.num_layers, hkv, cache.block_size,
+                                         cfg.head_dim_padded)
     if torch.device(device).type != "cuda":
         return max(64, (512 << 20) // per_block)
     free, _total = torch.cuda.mem_get_info(torch.device(device))
@@ -91,7 +92,7 @@ class LLMEngine:
         if comm is not None and comm.world > 1:
             nb = comm.min_int(nb)  # every rank must admit identically
         self.kv = KVCache(mcfg.num_layers, nb, self.model.hkv, cfg.cache.block_size,
-                          mcfg.head_dim, device=dev)
+                          mcfg.head_dim_padded, device=dev)
         self.blocks = BlockManager(nb, cfg.cache.block_size, cfg.cache.enable_prefix_caching)
         self.scheduler = Scheduler(cfg.scheduler, self.blocks)
         self.runner = ModelRunner(self.model, self.kv, self.blocks, cfg.scheduler.max_num_seqs,

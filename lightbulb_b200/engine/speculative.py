@@ -244,7 +244,7 @@ def attach_speculative(engine, draft_model, draft_cfg, k: int = 4, num_blocks: i
     c = engine.cfg
     nb = num_blocks or max(64, engine.blocks.num_blocks // 2)
     kv = KVCache(draft_cfg.num_layers, nb, draft_model.hkv, c.cache.block_size,
-                 draft_cfg.head_dim, device=draft_model.device)
+                 draft_cfg.head_dim_padded, device=draft_model.device)
     dbm = BlockManager(nb, c.cache.block_size, enable_prefix=False)
     runner = ModelRunner(draft_model, kv, dbm, c.scheduler.max_num_seqs,
                          c.scheduler.max_num_batched_tokens + c.scheduler.max_num_seqs * (k + 1),

@@ -60,6 +60,18 @@ class QuantWeight:
                            self.scales[:, k0 // self.group:k1 // self.group],
                            self.offsets[:, k0 // self.group:k1 // self.group], b, self.group)
 
+    def pad_head_rows(self, n_heads: int, d: int, dp: int) -> "QuantWeight":
+        """Insert all-zero rows (q = 0, scale = offset = 0 -> w = 0) after each head's d rows."""
+        if d == dp:
+            return self
+
+        def pad(t):
+            out = torch.zeros((n_heads, dp) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+            out[:, :d] = t.reshape((n_heads, d) + tuple(t.shape[1:]))
+            return out.reshape((n_heads * dp,) + tuple(t.shape[1:]))
+        return QuantWeight(pad(self.qw), pad(self.scales), pad(self.offsets), self.bits,
+                           self.group)
+
     def unpack(self) -> torch.Tensor:
         """Integer values [N, K] (int16)."""
         if self.bits == 4:

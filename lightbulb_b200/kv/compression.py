@@ -34,6 +34,10 @@ class H2OPolicy:
         self.score = torch.zeros(kv.num_blocks * kv.block_size, dtype=torch.float32,
                                  device=kv.storage.device)
         engine.model.h2o = self
+        # softmax scale of the model's attention (1 / sqrt(true head_dim) for padded heads);
+        # None -> 1 / sqrt(width of q)
+        cfg = getattr(engine.model, "cfg", None)
+        self.scale = 1.0 / (cfg.head_dim ** 0.5) if cfg is not None else None
         self.compactions = 0
 
     def before_step(self, so) -> None:
@@ -45,9 +49,10 @@ class H2OPolicy:
 
     # called from the model on the last layer (inside the step, graph-capturable)
     def accumulate(self, q, k_cache, block_tables, seq_lens):
+        scale = self.scale if self.scale is not None else 1.0 / (q.shape[-1] ** 0.5)
         if q.is_cuda:
             ops._need_c().h2o_accumulate(q, k_cache, block_tables, seq_lens, self.score,
-                                         self.decay)
+                                         self.decay, scale)
             ops.launch_counter_add(1)
             return
         bs = k_cache.shape[2]
@@ -59,7 +64,7 @@ class H2OPolicy:
             k = k_cache[blk].permute(0, 2, 1, 3).reshape(nb * bs, k_cache.shape[1], -1)[:L]
             g = q.shape[1] // k.shape[1]
             kk = k.float().repeat_interleave(g, dim=1)
-            s = torch.einsum("hd,khd->hk", q[i].float(), kk) / (q.shape[-1] ** 0.5)
+            s = torch.einsum("hd,khd->hk", q[i].float(), kk) * scale
             p = torch.softmax(s, dim=-1).sum(0)
             self.score[slots] = self.score[slots] * self.decay + p
 

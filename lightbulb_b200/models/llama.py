@@ -16,6 +16,8 @@ Tensor parallelism (``comm`` hooks) is injected by :mod:`lightbulb_b200.parallel
 """
 from __future__ import annotations
 
+import math
+
 from dataclasses import dataclass
 from typing import Callable, List, Optional
 
@@ -98,7 +100,8 @@ class LlamaModel:
         self.tp_rank, self.tp_size = tp_rank, tp_size
         self.hq = cfg.num_heads // tp_size
         self.hkv = max(1, cfg.num_kv_heads // tp_size)
-        self.d = cfg.head_dim
+        self.d = cfg.head_dim_padded          # device head width (narrow heads zero-padded)
+        self.scale = 1.0 / math.sqrt(cfg.head_dim)
         self.group = self.hq // self.hkv
         self.device = packed["embed"].device
         mp = max_positions or cfg.max_position_embeddings
@@ -140,7 +143,7 @@ class LlamaModel:
             q = qkv[:, :hq * d].view(T, hq, d)
             ops.paged_attention(q, kv.k[i], kv.v[i], b.block_tables, b.seq_lens, b.cu_q,
                                 attn.view(T, hq, d), self.group, decode=True,
-                                num_splits=b.decode_splits)
+                                num_splits=b.decode_splits, scale=self.scale)
             F.gemm_scatter(attn, L["o"], R)
             F.norm_gather(L["ln_post"], R, eps)
             act = F.gemm_consume(h, L["gate_up"], mode=ops.EPI_SWIGLU)
@@ -172,13 +175,13 @@ class LlamaModel:
             if nd > 0:
                 ops.paged_attention(q, kv.k[i], kv.v[i], b.block_tables[:nd], b.seq_lens[:nd],
                                     b.cu_q[:nd + 1], a3, self.group, decode=True,
-                                    num_splits=b.decode_splits,
+                                    num_splits=b.decode_splits, scale=self.scale,
                                     seq_lens_cpu=b.seq_lens_cpu, cu_q_cpu=b.cu_q_cpu)
             if b.tile_seq is not None and b.tile_seq.numel() > 0:
                 ops.paged_attention(q, kv.k[i], kv.v[i], b.block_tables, b.seq_lens, b.cu_q,
                                     a3, self.group, decode=False, tile_seq=b.tile_seq,
                                     tile_row0=b.tile_row0, seq_lens_cpu=b.seq_lens_cpu,
-                                    cu_q_cpu=b.cu_q_cpu)
+                                    cu_q_cpu=b.cu_q_cpu, scale=self.scale)
             if self.h2o is not None and nd > 0 and i == len(self.layers) - 1:
                 self.h2o.accumulate(q[:nd], kv.k[i], b.block_tables[:nd], b.seq_lens[:nd])
             o = ops.gemm(attn, L["o"])

@@ -42,15 +42,17 @@ def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.T
 
 
 def attention_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_pos: torch.Tensor,
-                  k_pos: Optional[torch.Tensor] = None, causal: bool = True) -> torch.Tensor:
-    """fp32 GQA attention.  q: [Tq, Hq, D]; k, v: [Tk, Hkv, D]; positions give the causal mask."""
+                  k_pos: Optional[torch.Tensor] = None, causal: bool = True,
+                  scale: Optional[float] = None) -> torch.Tensor:
+    """fp32 GQA attention.  q: [Tq, Hq, D]; k, v: [Tk, Hkv, D]; positions give the causal mask;
+    scale defaults to 1 / sqrt(D)."""
     tq, hq, d = q.shape
     tk, hkv, _ = k.shape
     g = hq // hkv
     qf, kf, vf = q.float(), k.float(), v.float()
     kf = kf.repeat_interleave(g, dim=1)
     vf = vf.repeat_interleave(g, dim=1)
-    s = torch.einsum("qhd,khd->hqk", qf, kf) / math.sqrt(d)
+    s = torch.einsum("qhd,khd->hqk", qf, kf) * (scale if scale is not None else 1.0 / math.sqrt(d))
     if causal:
         if k_pos is None:
             k_pos = torch.arange(tk)

@@ -147,6 +147,26 @@ def tp_head_ranges(cfg: ModelConfig, rank: int, world: int):
     return (q0, hq), (k0, hk)
 
 
+def pad_head_rows(w: torch.Tensor, n_heads: int, d: int, dp: int) -> torch.Tensor:
+    """[n_heads * d, K] -> [n_heads * dp, K] with zero rows after each head's d rows."""
+    if d == dp:
+        return w
+    k = w.shape[1]
+    out = torch.zeros(n_heads, dp, k, dtype=w.dtype, device=w.device)
+    out[:, :d] = w.reshape(n_heads, d, k)
+    return out.reshape(n_heads * dp, k)
+
+
+def pad_head_cols(w: torch.Tensor, n_heads: int, d: int, dp: int) -> torch.Tensor:
+    """[H, n_heads * d] -> [H, n_heads * dp] with zero columns after each head's d columns."""
+    if d == dp:
+        return w
+    h = w.shape[0]
+    out = torch.zeros(h, n_heads, dp, dtype=w.dtype, device=w.device)
+    out[:, :, :d] = w.reshape(h, n_heads, d)
+    return out.reshape(h, n_heads * dp)
+
+
 def pack_layer(cfg: ModelConfig, w: Dict[str, torch.Tensor], i: int, rank: int = 0,
                world: int = 1, dtype=torch.bfloat16, device="cpu") -> Dict[str, torch.Tensor]:
     p = f"model.layers.{i}."
@@ -166,6 +186,10 @@ def pack_layer(cfg: ModelConfig, w: Dict[str, torch.Tensor], i: int, rank: int =
     def dev(t):
         return t.to(device=device, dtype=dtype).contiguous()
 
+    dp = cfg.head_dim_padded
+    qw, kw, vw = (pad_head_rows(qw, hq, d, dp), pad_head_rows(kw, hk, d, dp),
+                  pad_head_rows(vw, hk, d, dp))
+    ow = pad_head_cols(ow, hq, d, dp)
     return {
         "ln_in": dev(w[p + "input_layernorm.weight"]),
         "ln_post": dev(w[p + "post_attention_layernorm.weight"]),
@@ -242,6 +266,13 @@ def pack_layer_quant(cfg: ModelConfig, lw: Dict[str, object], i: int, rank: int 
     def nrm(name):
         return lw[p + name].to(device=device, dtype=torch.bfloat16).contiguous()
 
+    dp = cfg.head_dim_padded
+    if dp != d:
+        # narrow heads: zero rows per head in q/k/v (exact); o_proj's input groups would not
+        # line up with the padded head width, so it is kept dequantized (bf16)
+        qw, kw, vw = (qw.pad_head_rows(hq, d, dp), kw.pad_head_rows(hk, d, dp),
+                      vw.pad_head_rows(hk, d, dp))
+        ow = pad_head_cols(ow.to(device).dequantize(torch.bfloat16), hq, d, dp)
     return {"ln_in": nrm("input_layernorm.weight"), "ln_post": nrm("post_attention_layernorm.weight"),
             "qkv": dev(cat_rows([qw, kw, vw])), "o": dev(ow),
             "gate_up": dev(interleave_rows(gw, uw)), "down": dev(dw)}

@@ -228,20 +228,23 @@ def rope_table(max_pos: int, head_dim: int, theta: float, device) -> torch.Tenso
 def rope_kv(qkv: torch.Tensor, positions: torch.Tensor, slots: Optional[torch.Tensor],
             cos_sin: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, hq: int,
             hkv: int) -> None:
-    """Rotate q (in place) and k of ``qkv`` [T, (hq + 2 hkv) D] and write k, v to their slots."""
+    """Rotate q (in place) and k of ``qkv`` [T, (hq + 2 hkv) D] and write k, v to their slots.
+    D = the cache's head width; the rotation covers the first ``cos_sin.shape[1]`` lanes of
+    each head (the true head_dim when heads are zero-padded)."""
     if qkv.is_cuda:
         _need_c().rope_kv(qkv, positions, slots, cos_sin, k_cache, v_cache, hq, hkv,
                           scratch(qkv.device).err)
         _launches[0] += 1
         return
-    d = cos_sin.shape[1]
+    d = k_cache.shape[-1]           # head stride (padded width)
+    r = cos_sin.shape[1]            # rotary width (true head_dim)
     t = qkv.shape[0]
-    half = d // 2
+    half = r // 2
     cs = cos_sin[positions.long()]
     c, s = cs[:, None, :half], cs[:, None, half:]
     x = qkv[:, :(hq + hkv) * d].view(t, hq + hkv, d).float()
-    x1, x2 = x[..., :half], x[..., half:]
-    rot = torch.cat([x1 * c - x2 * s, x1 * s + x2 * c], -1).to(qkv.dtype)
+    x1, x2 = x[..., :half], x[..., half:r]
+    rot = torch.cat([x1 * c - x2 * s, x1 * s + x2 * c, x[..., r:]], -1).to(qkv.dtype)
     qkv[:, :hq * d].copy_(rot[:, :hq].reshape(t, -1))
     if slots is not None:
         bs = k_cache.shape[2]
@@ -275,10 +278,13 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
                     out: torch.Tensor, group: int, decode: bool,
                     tile_seq: Optional[torch.Tensor] = None,
                     tile_row0: Optional[torch.Tensor] = None, num_splits: int = 1,
-                    causal: bool = True, seq_lens_cpu=None, cu_q_cpu=None) -> torch.Tensor:
-    """q: [T, Hq, D] (may be a strided view of the QKV buffer); out: [T, Hq, D]."""
+                    causal: bool = True, seq_lens_cpu=None, cu_q_cpu=None,
+                    scale: Optional[float] = None) -> torch.Tensor:
+    """q: [T, Hq, D] (may be a strided view of the QKV buffer); out: [T, Hq, D].  ``scale``
+    defaults to 1 / sqrt(D) (pass 1 / sqrt(true head_dim) for zero-padded heads)."""
     d = q.shape[-1]
-    scale = 1.0 / math.sqrt(d)
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
     if q.is_cuda:
         C = _need_c()
         po = pl = None
@@ -309,7 +315,7 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
         k = k_cache[blocks].permute(0, 2, 1, 3).reshape(nb * bs, k_cache.shape[1], d)[:L]
         v = v_cache[blocks].permute(0, 2, 1, 3).reshape(nb * bs, v_cache.shape[1], d)[:L]
         qpos = torch.arange(L - (q1 - q0), L)
-        o = attention_ref(q[q0:q1], k, v, qpos, torch.arange(L), causal=causal)
+        o = attention_ref(q[q0:q1], k, v, qpos, torch.arange(L), causal=causal, scale=scale)
         out[q0:q1] = o.to(out.dtype)
     return out
 

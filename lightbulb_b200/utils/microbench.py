@@ -151,13 +151,17 @@ def trace_gemm(m, n, k, bt=0, splits=0):
     t0 = t[:, 0].min()
     names = ["start", "prologue", "acc_ready", "published", "synced", "reduced_stored",
              "exit"]
+    # second row (thread 0 of the epilogue): inside publish / reduce / store
+    names2 = ["tmem_to_smem", "bar", "bulk_issued", "bulk_done", "fetched", "reduced",
+              "tma_issue", "tma_done"]
     res = {"op": "gemm_trace", "m": m, "n": n, "k": k, "ctas": grid}
-    for i, nm in enumerate(names):
-        col = t[:, i]
-        ok = col > 0
-        if ok.any():
-            res[nm + "_us"] = round(float((col[ok] - t0).mean()) / 1e3, 2)
-            res[nm + "_max_us"] = round(float((col[ok] - t0).max()) / 1e3, 2)
+    t2 = t_all[grid:2 * grid].double()
+    for tab, nms in ((t, names), (t2, names2)):
+        for i, nm in enumerate(nms):
+            col = tab[:, i]
+            ok = col > 0
+            if ok.any():
+                res[nm + "_us"] = round(float((col[ok] - t0).mean()) / 1e3, 2)
     return res
 
 

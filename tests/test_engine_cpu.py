@@ -79,3 +79,29 @@ def test_eos_and_budget_truncation():
         eng.step()
     assert seq.finish_reason in ("length", "stop")
     assert len(seq.output_token_ids) <= 9
+
+
+import pytest  # noqa: E402
+
+
+@pytest.mark.parametrize("hidden,heads,kv", [(256, 4, 4), (384, 4, 2), (512, 4, 4)])
+def test_padded_head_widths_match_oracle(hidden, heads, kv):
+    # head_dim 64 (TinyLlama / Llama-3.2-1B), 96 (Phi-3-mini) and 128: heads are zero-padded
+    # to the 128-wide device layout; greedy output must follow the unpadded fp32 oracle
+    cfg = get_preset("tiny-test", hidden_size=hidden, num_heads=heads, num_kv_heads=kv,
+                     head_dim=hidden // heads)
+    assert cfg.head_dim == hidden // heads and cfg.head_dim_padded == 128
+    w = random_weights(cfg, seed=3, std=0.05)
+    w = {k: v.to(torch.bfloat16).float() for k, v in w.items()}
+    packed = pack_model(cfg, w, dtype=torch.bfloat16, device="cpu")
+    assert packed["layers"][0]["qkv"].shape[0] == (heads + 2 * kv) * 128
+    ecfg = EngineConfig(model=cfg, cache=CacheConfig(num_blocks=32, block_size=16),
+                        scheduler=SchedulerConfig(max_num_seqs=4, max_num_batched_tokens=64,
+                                                  chunk_size=32, max_model_len=256),
+                        use_cuda_graphs=False)
+    eng = LLMEngine(ecfg, packed)
+    ref = ReferenceLlama(cfg, w)
+    prompts = [list(range(5, 45)), [9, 8, 7]]
+    sp = SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True)
+    for p, s in zip(prompts, eng.generate(prompt_token_ids=prompts, params=sp)):
+        assert_greedy_consistent(ref, p, s.output_token_ids)

@@ -57,3 +57,30 @@ def test_engine_graph_vs_eager_identical():
     a = [s.output_token_ids for s in e1.generate(prompt_token_ids=prompts, params=sp)]
     b = [s.output_token_ids for s in e2.generate(prompt_token_ids=prompts, params=sp)]
     assert a == b
+
+
+@pytest.mark.parametrize("hidden,heads,kv", [(512, 8, 2), (384, 4, 4)])
+def test_engine_padded_heads_gpu(hidden, heads, kv):
+    # head_dim 64 (Llama-3.2-1B / TinyLlama) and 96 (Phi-3-mini) zero-padded to the 128-wide
+    # kernels: the GPU engine must follow the unpadded fp32 oracle
+    cfg = get_preset("tiny-test", hidden_size=hidden, intermediate_size=1024, num_heads=heads,
+                     num_kv_heads=kv, head_dim=hidden // heads, vocab_size=1024)
+    w = random_weights(cfg, seed=5, std=0.05)
+    w = {k: v.to(torch.bfloat16).float() for k, v in w.items()}
+    packed = pack_model(cfg, w, dtype=torch.bfloat16, device="cuda")
+    ecfg = EngineConfig(model=cfg, cache=CacheConfig(num_blocks=64, block_size=16),
+                        scheduler=SchedulerConfig(max_num_seqs=4, max_num_batched_tokens=96,
+                                                  chunk_size=48, max_model_len=512),
+                        use_cuda_graphs=True)
+    eng = LLMEngine(ecfg, packed)
+    ref = ReferenceLlama(cfg, w)
+    prompts = [list(range(3, 60)), [11, 12, 13]]
+    sp = SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True)
+    seqs = eng.generate(prompt_token_ids=prompts, params=sp)
+    ops.check_errors()
+    for p, s in zip(prompts, seqs):
+        ref.reset()
+        lg = ref.forward(torch.tensor(p + s.output_token_ids[:-1]))[len(p) - 1:]
+        for i, t in enumerate(s.output_token_ids):
+            top2 = torch.topk(lg[i], 2).values
+            assert int(torch.argmax(lg[i])) == t or (top2[0] - top2[1]) < 0.05
