@@ -35,7 +35,8 @@ void rs_norm_ag(int64_t rs_ptr, const c10::optional<at::Tensor>& x_in, at::Tenso
                 int64_t done_counter_ptr, int64_t rank, int64_t R, int64_t rows, double eps,
                 bool add_residual, at::Tensor& err, int64_t trace_ptr);
 void h2o_accumulate(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& block_tables,
-                    const at::Tensor& seq_lens, at::Tensor& score, double decay, double scale);
+                    const at::Tensor& seq_lens, at::Tensor& score, double decay, double scale,
+                    at::Tensor& ws_logits, at::Tensor& ws_part);
 void kv_compact(at::Tensor& storage, const at::Tensor& src, const at::Tensor& dst,
                 const c10::optional<at::Tensor>& score);
 void gemm_quant(const at::Tensor& X, const at::Tensor& qw, const at::Tensor& scales,

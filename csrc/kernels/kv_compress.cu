@@ -5,11 +5,11 @@
 // step, src/model/custom_transformer.rs:546-594) and token eviction by masking
 // (src/cache/parallel_cache_builder.rs:1451-1840).  Here both stay on the device:
 //
-//  * h2o_accumulate: one CTA per sequence recomputes the last layer's attention probabilities
-//    of every query head over the cached keys (two passes: row max / sum, then probabilities)
-//    and updates score[pos] = decay * score[pos] + sum over heads of p(head, pos).  Scores live
-//    in a pool parallel to the KV blocks ([num_blocks * block_size] fp32), so they move with
-//    their blocks.
+//  * h2o_accumulate: recomputes the last layer's attention probabilities of every query head
+//    over the cached keys (logits + per-tile softmax partials, then the combination) and
+//    updates score[pos] = decay * score[pos] + sum over heads of p(head, pos).  Scores live in a
+//    pool parallel to the KV blocks ([num_blocks * block_size] fp32), so they move with their
+//    blocks.
 //  * kv_compact: copies selected token slots (all layers, K and V, every KV head) to new slots,
 //    used after the host picks the tokens to keep (sinks + recent + heavy hitters).
 #include <ATen/cuda/CUDAContext.h>
@@ -21,61 +21,127 @@ namespace lb {
 
 constexpr int HD = 128;
 
-// q: [B, Hq, 128] (row stride q_stride), k_cache: [NB, Hkv, BS, 128]
-__global__ void __launch_bounds__(256) h2o_accumulate_kernel(
+// ---------------------------------------------------------------------------------------
+// H2O accumulation in two launches, both sized by the workspace (max sequences x max model
+// length), reading the live lengths from the device -- so they can be captured in the decode
+// CUDA graphs -- and deterministic (fixed reduction orders, no atomics).
+//
+//  h2o_logits_kernel  grid (key tiles, Hkv, B), 256 threads, one key per thread: the logits of
+//                     the G query heads of this KV head (q pre-scaled in shared memory) go to
+//                     ws_logits[b][h][key]; the tile's per-head max and sum of exp go to
+//                     ws_part[b][h][tile] = (m, l).
+//  h2o_accum_kernel   grid (key tiles, B): per head, M = max of the tiles' m and L = sum of
+//                     l * exp(m - M); then for every key p < len:
+//                     score[slot(p)] = decay * score[slot(p)] + sum_h exp(s_h(p) - M_h) / L_h.
+// ---------------------------------------------------------------------------------------
+constexpr int H2O_TILE = 256;
+constexpr int H2O_MAXG = 16;
+
+__global__ void __launch_bounds__(H2O_TILE) h2o_logits_kernel(
     const bf16* q, int q_stride, const bf16* k_cache, const int* block_tables, int bt_stride,
-    const int* seq_lens, float* score, int hq, int hkv, int bs, float scale, float decay) {
-  const int seq = blockIdx.x;
-  const int L = seq_lens[seq];
-  const int* bt = block_tables + static_cast<size_t>(seq) * bt_stride;
-  const int group = hq / hkv;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __shared__ float s_qf[HD];
-  __shared__ float red_m[8], red_s[8];
-  // decay every cached position once
-  for (int p = threadIdx.x; p < L; p += blockDim.x) {
-    const size_t slot = static_cast<size_t>(bt[p / bs]) * bs + p % bs;
-    score[slot] *= decay;
+    const int* seq_lens, float* ws_logits, float2* ws_part, int hq, int hkv, int bs, int lmax,
+    int tmax, float scale) {
+  const int tile = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int G = hq / hkv;
+  const int L = seq_lens[b];
+  const int p0 = tile * H2O_TILE;
+  float2* part = ws_part + (static_cast<size_t>(b) * hq + kvh * G) * tmax + tile;
+  if (p0 >= L) {
+    if (threadIdx.x < G) part[static_cast<size_t>(threadIdx.x) * tmax] = make_float2(-INFINITY, 0.f);
+    return;
+  }
+  __shared__ float sq[H2O_MAXG][HD];
+  __shared__ float red[8][H2O_MAXG];
+  for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
+    const int g = i / HD, d = i % HD;
+    sq[g][d] = __bfloat162float(q[static_cast<size_t>(b) * q_stride + (kvh * G + g) * HD + d]) *
+               scale;
   }
   __syncthreads();
-  for (int h = 0; h < hq; ++h) {
-    const int kvh = h / group;
-    for (int d = threadIdx.x; d < HD; d += blockDim.x)
-      s_qf[d] = __bfloat162float(q[static_cast<size_t>(seq) * q_stride + h * HD + d]) * scale;
-    __syncthreads();
-    // pass 1: max and sum of exp over keys (each warp takes keys w, w+8, ...)
-    float m = -INFINITY, ssum = 0.f;
-    for (int p = warp; p < L; p += 8) {
-      const size_t slot = static_cast<size_t>(bt[p / bs]) * bs + p % bs;
-      const bf16* kr = k_cache + (slot / bs * hkv + kvh) * bs * HD + (slot % bs) * HD;
-      float dot = 0.f;
-      for (int d = lane; d < HD; d += 32) dot += s_qf[d] * __bfloat162float(kr[d]);
-      dot = warp_sum(dot);
-      const float mn = fmaxf(m, dot);
-      ssum = ssum * __expf(m - mn) + __expf(dot - mn);
-      m = mn;
+  const int p = p0 + threadIdx.x;
+  const bool valid = p < L;
+  float acc[H2O_MAXG];
+#pragma unroll
+  for (int g = 0; g < H2O_MAXG; ++g) acc[g] = 0.f;
+  if (valid) {
+    const int* bt = block_tables + static_cast<size_t>(b) * bt_stride;
+    const int blk = bt[p / bs];
+    const uint4* kr = reinterpret_cast<const uint4*>(
+        k_cache + ((static_cast<size_t>(blk) * hkv + kvh) * bs + p % bs) * HD);
+#pragma unroll 4
+    for (int c = 0; c < HD / 8; ++c) {
+      const uint4 v = __ldg(kr + c);
+      const bf16* kv8 = reinterpret_cast<const bf16*>(&v);
+      float kf[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) kf[j] = __bfloat162float(kv8[j]);
+#pragma unroll
+      for (int g = 0; g < H2O_MAXG; ++g) {
+        if (g < G) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[g] = fmaf(sq[g][c * 8 + j], kf[j], acc[g]);
+        }
+      }
     }
-    if (lane == 0) {
-      red_m[warp] = m;
-      red_s[warp] = ssum;
-    }
-    __syncthreads();
-    float M = -INFINITY;
-    for (int w = 0; w < 8; ++w) M = fmaxf(M, red_m[w]);
-    float S = 0.f;
-    for (int w = 0; w < 8; ++w) S += red_m[w] == -INFINITY ? 0.f : red_s[w] * __expf(red_m[w] - M);
-    const float inv = S > 0.f ? 1.f / S : 0.f;
-    // pass 2: accumulate probabilities (one lane per key after the warp dot product)
-    for (int p = warp; p < L; p += 8) {
-      const size_t slot = static_cast<size_t>(bt[p / bs]) * bs + p % bs;
-      const bf16* kr = k_cache + (slot / bs * hkv + kvh) * bs * HD + (slot % bs) * HD;
-      float dot = 0.f;
-      for (int d = lane; d < HD; d += 32) dot += s_qf[d] * __bfloat162float(kr[d]);
-      dot = warp_sum(dot);
-      if (lane == 0) score[slot] += __expf(dot - M) * inv;
-    }
-    __syncthreads();
   }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* lrow = ws_logits + (static_cast<size_t>(b) * hq + kvh * G) * lmax;
+  for (int g = 0; g < G; ++g) {
+    if (valid) lrow[static_cast<size_t>(g) * lmax + p] = acc[g];
+    const float m = warp_max(valid ? acc[g] : -INFINITY);
+    if (lane == 0) red[warp][g] = m;
+  }
+  __syncthreads();
+  float M[H2O_MAXG];
+  for (int g = 0; g < G; ++g) {
+    float m = -INFINITY;
+    for (int w = 0; w < 8; ++w) m = fmaxf(m, red[w][g]);
+    M[g] = m;
+  }
+  __syncthreads();
+  for (int g = 0; g < G; ++g) {
+    const float e = warp_sum(valid ? __expf(acc[g] - M[g]) : 0.f);
+    if (lane == 0) red[warp][g] = e;
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    const int g = threadIdx.x;
+    float l = 0.f;
+    for (int w = 0; w < 8; ++w) l += red[w][g];
+    part[static_cast<size_t>(g) * tmax] = make_float2(M[g], l);
+  }
+}
+
+__global__ void __launch_bounds__(H2O_TILE) h2o_accum_kernel(
+    const float* ws_logits, const float2* ws_part, const int* block_tables, int bt_stride,
+    const int* seq_lens, float* score, int hq, int bs, int lmax, int tmax, float decay) {
+  const int tile = blockIdx.x, b = blockIdx.y;
+  const int L = seq_lens[b];
+  const int p0 = tile * H2O_TILE;
+  if (p0 >= L) return;
+  extern __shared__ float s_ml[];  // [hq] max, [hq] 1 / sum
+  const int ntiles = (L + H2O_TILE - 1) / H2O_TILE;
+  for (int h = threadIdx.x; h < hq; h += blockDim.x) {
+    const float2* part = ws_part + (static_cast<size_t>(b) * hq + h) * tmax;
+    float M = -INFINITY;
+    for (int t = 0; t < ntiles; ++t) M = fmaxf(M, part[t].x);
+    float S = 0.f;
+    for (int t = 0; t < ntiles; ++t) {
+      const float2 v = part[t];
+      if (v.y > 0.f) S += v.y * __expf(v.x - M);
+    }
+    s_ml[h] = M;
+    s_ml[hq + h] = S > 0.f ? 1.f / S : 0.f;
+  }
+  __syncthreads();
+  const int p = p0 + threadIdx.x;
+  if (p >= L) return;
+  const float* lcol = ws_logits + static_cast<size_t>(b) * hq * lmax + p;
+  float sum = 0.f;
+  for (int h = 0; h < hq; ++h) sum += __expf(lcol[static_cast<size_t>(h) * lmax] - s_ml[h]) * s_ml[hq + h];
+  const int* bt = block_tables + static_cast<size_t>(b) * bt_stride;
+  const size_t slot = static_cast<size_t>(bt[p / bs]) * bs + p % bs;
+  score[slot] = score[slot] * decay + sum;
 }
 
 // storage: [layers, 2, NB, Hkv, BS, 128]; copy token slot src[i] -> dst[i] for every layer/head.
@@ -104,16 +170,36 @@ __global__ void kv_compact_kernel(bf16* storage, const int* src, const int* dst,
   if (score != nullptr && threadIdx.x == 0) score[t] = score[s];
 }
 
+// q: [B, Hq, 128] (row stride q.stride(0)); k_cache: [NB, Hkv, BS, 128]; ws_logits: fp32
+// [>= B, Hq, Lmax]; ws_part: fp32 [>= B, Hq, ceil(Lmax / 256), 2].  Every seq_len <= Lmax.
 void h2o_accumulate(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& block_tables,
-                    const at::Tensor& seq_lens, at::Tensor& score, double decay, double scale) {
+                    const at::Tensor& seq_lens, at::Tensor& score, double decay, double scale,
+                    at::Tensor& ws_logits, at::Tensor& ws_part) {
   const int B = seq_lens.size(0);
   if (B == 0) return;
   TORCH_CHECK(q.size(-1) == HD && k_cache.size(3) == HD, "h2o: head dim 128");
-  h2o_accumulate_kernel<<<B, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+  const int hq = q.size(1), hkv = k_cache.size(1);
+  TORCH_CHECK(hq % hkv == 0 && hq / hkv <= H2O_MAXG, "h2o: group size <= 16");
+  TORCH_CHECK(ws_logits.dim() == 3 && ws_logits.size(0) >= B && ws_logits.size(1) == hq &&
+                  ws_logits.is_contiguous() && ws_logits.scalar_type() == at::kFloat,
+              "h2o: logits workspace [>= B, Hq, Lmax] fp32");
+  const int lmax = ws_logits.size(2);
+  const int tmax = (lmax + H2O_TILE - 1) / H2O_TILE;
+  TORCH_CHECK(ws_part.numel() >= static_cast<int64_t>(B) * hq * tmax * 2 &&
+                  ws_part.is_contiguous() && ws_part.scalar_type() == at::kFloat,
+              "h2o: partials workspace");
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  float2* part = reinterpret_cast<float2*>(ws_part.data_ptr<float>());
+  h2o_logits_kernel<<<dim3(tmax, hkv, B), H2O_TILE, 0, st>>>(
       reinterpret_cast<const bf16*>(q.data_ptr()), q.stride(0),
       reinterpret_cast<const bf16*>(k_cache.data_ptr()), block_tables.data_ptr<int>(),
-      block_tables.stride(0), seq_lens.data_ptr<int>(), score.data_ptr<float>(), q.size(1),
-      k_cache.size(1), k_cache.size(2), static_cast<float>(scale), static_cast<float>(decay));
+      block_tables.stride(0), seq_lens.data_ptr<int>(), ws_logits.data_ptr<float>(), part, hq,
+      hkv, k_cache.size(2), lmax, tmax, static_cast<float>(scale));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  h2o_accum_kernel<<<dim3(tmax, B), H2O_TILE, 2 * hq * sizeof(float), st>>>(
+      ws_logits.data_ptr<float>(), part, block_tables.data_ptr<int>(), block_tables.stride(0),
+      seq_lens.data_ptr<int>(), score.data_ptr<float>(), hq, k_cache.size(2), lmax, tmax,
+      static_cast<float>(decay));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

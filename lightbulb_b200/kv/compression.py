@@ -38,6 +38,14 @@ class H2OPolicy:
         # None -> 1 / sqrt(width of q)
         cfg = getattr(engine.model, "cfg", None)
         self.scale = 1.0 / (cfg.head_dim ** 0.5) if cfg is not None else None
+        self._ws = None  # device workspaces of h2o_accumulate (logits, softmax partials)
+        model = engine.model
+        ecfg = getattr(engine, "cfg", None)
+        if kv.storage.is_cuda and ecfg is not None and hasattr(model, "hq"):
+            # allocated before any decode graph is captured
+            bs = kv.block_size
+            lmax = ((ecfg.scheduler.max_model_len + bs - 1) // bs + 1) * bs
+            self._alloc(ecfg.scheduler.max_num_seqs, model.hq, lmax, kv.storage.device)
         self.compactions = 0
 
     def before_step(self, so) -> None:
@@ -51,9 +59,10 @@ class H2OPolicy:
     def accumulate(self, q, k_cache, block_tables, seq_lens):
         scale = self.scale if self.scale is not None else 1.0 / (q.shape[-1] ** 0.5)
         if q.is_cuda:
+            ws_l, ws_p = self._workspaces(q, block_tables, k_cache.shape[2])
             ops._need_c().h2o_accumulate(q, k_cache, block_tables, seq_lens, self.score,
-                                         self.decay, scale)
-            ops.launch_counter_add(1)
+                                         self.decay, scale, ws_l, ws_p)
+            ops.launch_counter_add(2)
             return
         bs = k_cache.shape[2]
         for i in range(seq_lens.shape[0]):
@@ -67,6 +76,22 @@ class H2OPolicy:
             s = torch.einsum("hd,khd->hk", q[i].float(), kk) * scale
             p = torch.softmax(s, dim=-1).sum(0)
             self.score[slots] = self.score[slots] * self.decay + p
+
+    def _alloc(self, bmax, hq, lmax, device):
+        tmax = (lmax + 255) // 256
+        self._ws = (torch.empty(bmax, hq, lmax, dtype=torch.float32, device=device),
+                    torch.empty(bmax, hq, tmax, 2, dtype=torch.float32, device=device))
+
+    def _workspaces(self, q, block_tables, bs):
+        """Logits [max seqs, Hq, max len] and softmax partials, sized from the engine limits at
+        construction (the kernels read the live lengths on the device, so the decode CUDA
+        graphs can capture them); grown here only for callers outside those limits."""
+        lmax = block_tables.shape[1] * bs
+        ws = self._ws
+        if ws is None or ws[0].shape[0] < q.shape[0] or ws[0].shape[2] < lmax or \
+                ws[0].shape[1] != q.shape[1]:
+            self._alloc(q.shape[0], q.shape[1], lmax, q.device)
+        return self._ws
 
     def after_step(self, engine) -> None:
         bs = engine.kv.block_size
@@ -119,6 +144,22 @@ class StreamingPolicy:
     def __init__(self, engine, sinks: int = 4, window: int = 2048):
         self.sinks, self.window = sinks, window
         self.evictions = 0
+
+    def _alloc(self, bmax, hq, lmax, device):
+        tmax = (lmax + 255) // 256
+        self._ws = (torch.empty(bmax, hq, lmax, dtype=torch.float32, device=device),
+                    torch.empty(bmax, hq, tmax, 2, dtype=torch.float32, device=device))
+
+    def _workspaces(self, q, block_tables, bs):
+        """Logits [max seqs, Hq, max len] and softmax partials, sized from the engine limits at
+        construction (the kernels read the live lengths on the device, so the decode CUDA
+        graphs can capture them); grown here only for callers outside those limits."""
+        lmax = block_tables.shape[1] * bs
+        ws = self._ws
+        if ws is None or ws[0].shape[0] < q.shape[0] or ws[0].shape[2] < lmax or \
+                ws[0].shape[1] != q.shape[1]:
+            self._alloc(q.shape[0], q.shape[1], lmax, q.device)
+        return self._ws
 
     def after_step(self, engine) -> None:
         bm = engine.blocks

@@ -2,6 +2,9 @@
 
     python -m lightbulb_b200.utils.microbench decode --batch 256 --ctx 1200 [--tp 1]
     python -m lightbulb_b200.utils.microbench gemm --m 256 --n 4096 --k 4096
+    python -m lightbulb_b200.utils.microbench prefill --batch 4 --chunk 512 --ctx 4096
+    python -m lightbulb_b200.utils.microbench small_ops --batch 256
+    python -m lightbulb_b200.utils.microbench kv_ops --batch 16 --ctx 4096
 
 Reports time, achieved bytes/s or FLOP/s and the fraction of the measured roofline
 (``MEASURED_PEAKS.json`` when present: copy bandwidth and cuBLAS bf16 throughput).
@@ -189,6 +192,112 @@ def bench_decode_attn(batch, ctx, hq, hkv, bs=16, splits=None, iters=20):
             "frac_of_" + src: round(byts / bw * 1e6 / us, 3)}
 
 
+def bench_prefill_attn(batch, chunk, ctx, hq, hkv, bs=16, iters=10):
+    """Chunked-prefill attention: ``batch`` sequences, each a chunk of ``chunk`` new query
+    tokens at the end of a ``ctx``-token paged context (causal)."""
+    from ..models.llama import prefill_tiles
+    bw, fl, src = peaks()
+    d = 128
+    nb_per = (ctx + bs - 1) // bs
+    nblocks = batch * nb_per + 8
+    kc = torch.empty(nblocks, hkv, bs, d, device="cuda", dtype=torch.bfloat16).normal_()
+    vc = torch.empty_like(kc).normal_()
+    bt = torch.randperm(nblocks, device="cuda")[:batch * nb_per].view(batch, nb_per).int()
+    sl = torch.full((batch,), ctx, dtype=torch.int32, device="cuda")
+    cu = [i * chunk for i in range(batch + 1)]
+    q = torch.randn(batch * chunk, hq, d, device="cuda").to(torch.bfloat16)
+    out = torch.empty_like(q)
+    ts, tr = prefill_tiles(cu, 0, hq // hkv)
+    tile_seq = torch.tensor(ts, dtype=torch.int32, device="cuda")
+    tile_row0 = torch.tensor(tr, dtype=torch.int32, device="cuda")
+    cu_t = torch.tensor(cu, dtype=torch.int32, device="cuda")
+    sl_cpu, cu_cpu = sl.cpu(), torch.tensor(cu, dtype=torch.int32)
+
+    def run():
+        ops.paged_attention(q, kc, vc, bt, sl, cu_t, out, hq // hkv, decode=False,
+                            tile_seq=tile_seq, tile_row0=tile_row0,
+                            seq_lens_cpu=sl_cpu, cu_q_cpu=cu_cpu)
+
+    us = time_graph(run, calls=iters)
+    pairs = sum(ctx - chunk + i + 1 for i in range(chunk)) * batch   # causal (q, k) pairs
+    flops = 4 * pairs * hq * d
+    byts = batch * ctx * hkv * d * 2 * 2 + 2 * q.numel() * 2
+    t_roof = max(flops / fl, byts / bw) * 1e6
+    return {"op": "attn_prefill", "batch": batch, "chunk": chunk, "ctx": ctx, "hq": hq,
+            "hkv": hkv, "us": round(us, 2), "tflops": round(flops / us / 1e6, 1),
+            "roofline_us": round(t_roof, 2), "frac_of_" + src: round(t_roof / us, 3)}
+
+
+def bench_small_ops(batch, model="llama3-8b"):
+    """Elementwise / sampling kernels of one decode step at ``batch`` tokens."""
+    from ..config import get_preset
+    bw, fl, src = peaks()
+    cfg = get_preset(model)
+    h, d = cfg.hidden_size, 128
+    hq, hkv = cfg.num_heads, cfg.num_kv_heads
+    rows = []
+    x = torch.randn(batch, h, device="cuda").to(torch.bfloat16)
+    r = torch.randn(batch, h, device="cuda").to(torch.bfloat16)
+    w = torch.ones(h, device="cuda", dtype=torch.bfloat16)
+    us = time_graph(lambda: ops.rmsnorm(x, w, 1e-5, residual=r), 50)
+    rows.append({"op": "rmsnorm_add", "us": round(us, 2),
+                 "frac_of_" + src: round(batch * h * 2 * 4 / bw * 1e6 / us, 3)})
+    emb = torch.randn(cfg.vocab_size, h, device="cuda").to(torch.bfloat16)
+    ids = torch.randint(0, cfg.vocab_size, (batch,), device="cuda", dtype=torch.int32)
+    us = time_graph(lambda: ops.embedding(ids, emb), 50)
+    rows.append({"op": "embedding", "us": round(us, 2)})
+    qkv = torch.randn(batch, (hq + 2 * hkv) * d, device="cuda").to(torch.bfloat16)
+    pos = torch.randint(0, 4000, (batch,), dtype=torch.int32, device="cuda")
+    slots = torch.randperm(batch * 16, device="cuda")[:batch].int()
+    cs = ops.rope_table(4096, d, cfg.rope_theta, "cuda")
+    kc = torch.zeros(batch, hkv, 16, d, device="cuda", dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    us = time_graph(lambda: ops.rope_kv(qkv, pos, slots, cs, kc, vc, hq, hkv), 50)
+    rows.append({"op": "rope_kv", "us": round(us, 2)})
+    logits = torch.randn(batch, cfg.vocab_size, device="cuda")
+    t = torch.full((batch,), 0.8, device="cuda")
+    tk = torch.full((batch,), 50, dtype=torch.int32, device="cuda")
+    tp = torch.full((batch,), 0.9, device="cuda")
+    seeds = torch.arange(batch, dtype=torch.int64, device="cuda")
+    us = time_graph(lambda: ops.sample(logits, t, tk, tp, seeds), 20)
+    rows.append({"op": "sample_topk_topp", "us": round(us, 2),
+                 "frac_of_" + src: round(logits.numel() * 4 / bw * 1e6 / us, 3)})
+    z = torch.zeros(batch, device="cuda")
+    zi = torch.zeros(batch, dtype=torch.int32, device="cuda")
+    us = time_graph(lambda: ops.sample(logits, z, zi, z + 1, seeds), 20)
+    rows.append({"op": "sample_greedy", "us": round(us, 2),
+                 "frac_of_" + src: round(logits.numel() * 4 / bw * 1e6 / us, 3)})
+    return rows
+
+
+def bench_kv_ops(batch, ctx, hq=32, hkv=8, layers=32, bs=16):
+    """H2O attention-mass accumulation (last layer) and KV compaction of ``ctx`` tokens."""
+    from .. import _C
+    bw, fl, src = peaks()
+    d = 128
+    nb_per = (ctx + bs - 1) // bs
+    nblocks = batch * nb_per + 8
+    kc = torch.empty(nblocks, hkv, bs, d, device="cuda", dtype=torch.bfloat16).normal_()
+    bt = torch.randperm(nblocks, device="cuda")[:batch * nb_per].view(batch, nb_per).int()
+    sl = torch.full((batch,), ctx, dtype=torch.int32, device="cuda")
+    q = torch.randn(batch, hq, d, device="cuda").to(torch.bfloat16)
+    score = torch.zeros(nblocks * bs, device="cuda")
+    wl = torch.empty(batch, hq, nb_per * bs, device="cuda")
+    wp = torch.empty(batch, hq, (nb_per * bs + 255) // 256, 2, device="cuda")
+    us = time_graph(lambda: _C.h2o_accumulate(q, kc, bt, sl, score, 0.95, d ** -0.5, wl, wp), 10)
+    rows = [{"op": "h2o_accumulate", "batch": batch, "ctx": ctx, "us": round(us, 2),
+             "gbs": round(batch * ctx * hkv * d * 2 * 2 / us / 1e3, 1)}]
+    storage = torch.zeros(layers, 2, nblocks, hkv, bs, d, device="cuda", dtype=torch.bfloat16)
+    n = batch * (ctx // 2)
+    src_s = torch.randperm(nblocks * bs, device="cuda")[:n].int()
+    dst_s = torch.randperm(nblocks * bs, device="cuda")[:n].int()
+    us = time_graph(lambda: _C.kv_compact(storage, src_s, dst_s, score), 5)
+    byts = n * layers * 2 * hkv * d * 2 * 2
+    rows.append({"op": "kv_compact", "tokens": n, "us": round(us, 2),
+                 "gbs": round(byts / us / 1e3, 1), "frac_of_" + src: round(byts / bw * 1e6 / us, 3)})
+    return rows
+
+
 def bench_decode(batch, ctx, tp=1, model="llama3-8b"):
     from ..config import get_preset
     cfg = get_preset(model)
@@ -228,7 +337,9 @@ def bench_decode(batch, ctx, tp=1, model="llama3-8b"):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["decode", "gemm", "attn", "gemm_trace", "gemm_quant"])
+    ap.add_argument("what", choices=["decode", "gemm", "attn", "gemm_trace", "gemm_quant",
+                                     "prefill", "small_ops", "kv_ops"])
+    ap.add_argument("--chunk", type=int, default=512)
     ap.add_argument("--kind", default="awq", choices=["awq", "q4k", "q80"])
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--ctx", type=int, default=1200)
@@ -251,6 +362,12 @@ def main(argv=None):
         rows = [trace_gemm(a.m, a.n, a.k, a.bt, a.splits)]
     elif a.what == "gemm":
         rows = [bench_gemm(a.m, a.n, a.k, bt=a.bt, splits=a.splits)]
+    elif a.what == "prefill":
+        rows = [bench_prefill_attn(a.batch, a.chunk, a.ctx, a.hq, a.hkv)]
+    elif a.what == "small_ops":
+        rows = bench_small_ops(a.batch, a.model)
+    elif a.what == "kv_ops":
+        rows = bench_kv_ops(a.batch, a.ctx, a.hq, a.hkv)
     else:
         rows = [bench_decode_attn(a.batch, a.ctx, a.hq, a.hkv,
                                   splits=a.splits if a.splits else None)]

@@ -25,21 +25,23 @@ def _engine(w, cfg, **cache):
     return LLMEngine(ecfg, packed), packed
 
 
-def test_h2o_accumulate_matches_cpu():
+@pytest.mark.parametrize("hq,hkv,L", [(8, 2, [5, 40, 130]), (32, 8, [300, 700, 17]),
+                                      (16, 16, [1030, 1])])
+def test_h2o_accumulate_matches_cpu(hq, hkv, L):
     from lightbulb_b200.kv.compression import H2OPolicy
     torch.manual_seed(0)
-    hq, hkv, bs = 8, 2, 16
-    L = [5, 40, 130]
-    nblocks = 32
+    bs = 16
+    nper = max((l + bs - 1) // bs for l in L)
+    nblocks = sum((l + bs - 1) // bs for l in L) + 4
     kc = torch.randn(nblocks, hkv, bs, 128).to(torch.bfloat16)
-    bt = torch.zeros(3, 10, dtype=torch.int32)
+    bt = torch.zeros(len(L), nper + 1, dtype=torch.int32)
     perm = torch.randperm(nblocks)
     o = 0
     for i, l in enumerate(L):
         n = (l + bs - 1) // bs
         bt[i, :n] = perm[o:o + n]
         o += n
-    q = torch.randn(3, hq, 128).to(torch.bfloat16)
+    q = torch.randn(len(L), hq, 128).to(torch.bfloat16)
     sl = torch.tensor(L, dtype=torch.int32)
 
     class E:  # minimal engine stub for the policy
