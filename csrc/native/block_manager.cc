@@ -220,6 +220,15 @@ class BlockManager {
     return out;
   }
 
+  // Return blocks from alloc_blocks that were never attached to a sequence (rollback).
+  void free_blocks(const std::vector<int>& blocks) {
+    for (int b : blocks) {
+      if (b < 0 || b >= static_cast<int>(ref_.size()) || ref_[b] <= 0)
+        throw std::runtime_error("free_blocks: block not held");
+      release(b);
+    }
+  }
+
   // Replace the table of `sid` with a compacted list of kept logical blocks (KV eviction:
   // the caller has moved surviving slots); blocks not kept are released.
   void set_blocks(int64_t sid, const std::vector<int>& blocks, int64_t num_tokens) {
@@ -407,6 +416,7 @@ void register_block_manager(py::module_& m) {
       .def("truncate", &BlockManager::truncate)
       .def("set_blocks", &BlockManager::set_blocks)
       .def("alloc_blocks", &BlockManager::alloc_blocks)
+      .def("free_blocks", &BlockManager::free_blocks)
       .def("free_sequence", &BlockManager::free_sequence)
       .def("block_table", &BlockManager::block_table)
       .def("num_tokens", &BlockManager::num_tokens)

@@ -145,22 +145,6 @@ class StreamingPolicy:
         self.sinks, self.window = sinks, window
         self.evictions = 0
 
-    def _alloc(self, bmax, hq, lmax, device):
-        tmax = (lmax + 255) // 256
-        self._ws = (torch.empty(bmax, hq, lmax, dtype=torch.float32, device=device),
-                    torch.empty(bmax, hq, tmax, 2, dtype=torch.float32, device=device))
-
-    def _workspaces(self, q, block_tables, bs):
-        """Logits [max seqs, Hq, max len] and softmax partials, sized from the engine limits at
-        construction (the kernels read the live lengths on the device, so the decode CUDA
-        graphs can capture them); grown here only for callers outside those limits."""
-        lmax = block_tables.shape[1] * bs
-        ws = self._ws
-        if ws is None or ws[0].shape[0] < q.shape[0] or ws[0].shape[2] < lmax or \
-                ws[0].shape[1] != q.shape[1]:
-            self._alloc(q.shape[0], q.shape[1], lmax, q.device)
-        return self._ws
-
     def after_step(self, engine) -> None:
         bm = engine.blocks
         bs = engine.kv.block_size
