@@ -103,12 +103,13 @@ class LlamaModel:
         self.d = cfg.head_dim_padded          # device head width (narrow heads zero-padded)
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
         self.group = self.hq // self.hkv
-        self.device = packed["embed"].device
+        ref = packed.get("embed")
+        self.device = (ref if ref is not None else packed["layers"][0]["qkv"]).device
         mp = max_positions or cfg.max_position_embeddings
         self.cos_sin = ops.rope_table(mp, cfg.head_dim, cfg.rope_theta, self.device)
         self.comm = comm  # tensor-parallel communicator (None = single GPU)
         self.h2o = None   # H2O policy: accumulates last-layer attention mass (kv/compression.py)
-        self.vocab_local = packed["lm_head"].shape[0]
+        self.vocab_local = packed["lm_head"].shape[0] if "lm_head" in packed else 0
 
     # ------------------------------------------------------------------------------
     def fused_ok(self, b: ForwardBatch) -> bool:
@@ -156,6 +157,14 @@ class LlamaModel:
         """Returns fp32 logits [len(b.logits_idx), vocab_local]."""
         if self.fused_ok(b):
             return self.forward_fused(b, kv)
+        return self.forward_stage(b, kv)
+
+    def forward_stage(self, b: ForwardBatch, kv: KVCache, x_in: Optional[torch.Tensor] = None,
+                      first: bool = True, last: bool = True) -> torch.Tensor:
+        """The layers this model holds, as one pipeline stage: ``first`` embeds ``b.input_ids``
+        (else ``x_in`` is the residual stream [T, H] from the previous stage), ``last`` applies
+        the final norm and the LM head (fp32 logits of ``b.logits_idx``); a middle or first
+        stage returns the residual stream after its last layer."""
         cfg = self.cfg
         T = b.num_tokens
         hq, hkv, d = self.hq, self.hkv, self.d
@@ -163,7 +172,10 @@ class LlamaModel:
         dev = self.device
         comm = self.comm
 
-        x = ops.embedding(b.input_ids, self.w["embed"])          # residual stream [T, H]
+        if first:
+            x = ops.embedding(b.input_ids, self.w["embed"])      # residual stream [T, H]
+        else:
+            x = x_in
         h = ops.rmsnorm(x, self.layers[0]["ln_in"], eps)
         attn = torch.empty(T, hq * d, dtype=torch.bfloat16, device=dev)
         nd = b.num_decode
@@ -182,7 +194,7 @@ class LlamaModel:
                                     a3, self.group, decode=False, tile_seq=b.tile_seq,
                                     tile_row0=b.tile_row0, seq_lens_cpu=b.seq_lens_cpu,
                                     cu_q_cpu=b.cu_q_cpu, scale=self.scale)
-            if self.h2o is not None and nd > 0 and i == len(self.layers) - 1:
+            if self.h2o is not None and nd > 0 and i == len(self.layers) - 1 and last:
                 self.h2o.accumulate(q[:nd], kv.k[i], b.block_tables[:nd], b.seq_lens[:nd])
             o = ops.gemm(attn, L["o"])
             if comm is not None:
@@ -192,7 +204,21 @@ class LlamaModel:
             dn = ops.gemm(act, L["down"])
             if comm is not None:
                 dn = comm.all_reduce(dn)
-            nw = self.layers[i + 1]["ln_in"] if i + 1 < len(self.layers) else self.w["norm"]
+            if i + 1 < len(self.layers):
+                nw = self.layers[i + 1]["ln_in"]
+            elif last:
+                nw = self.w["norm"]
+            else:
+                nw = self._ones(x.shape[1])  # stage boundary: only the residual update matters
             h = ops.rmsnorm(dn, nw, eps, residual=x)
+        if not last:
+            return x
         hl = h.index_select(0, b.logits_idx) if b.logits_idx.numel() != T else h
         return ops.gemm(hl, self.w["lm_head"], mode=ops.EPI_F32)
+
+    def _ones(self, n: int) -> torch.Tensor:
+        t = getattr(self, "_ones_cache", None)
+        if t is None or t.numel() != n:
+            t = torch.ones(n, dtype=torch.bfloat16, device=self.device)
+            self._ones_cache = t
+        return t
