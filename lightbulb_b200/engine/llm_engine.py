@@ -30,6 +30,7 @@ from ..models.llama import KVCache, LlamaModel
 from .model_runner import ModelRunner
 from .sampling import SamplingParams
 from .scheduler import Scheduler
+from ..utils import trace
 from .sequence import Sequence, SeqStatus, effective_generation_budget
 from .tokenizer import BaseTokenizer, ByteTokenizer, IncrementalDetokenizer
 
@@ -46,6 +47,7 @@ class RequestOutput:
     prompt_tokens: int = 0
     completion_tokens: int = 0
     cached_tokens: int = 0
+    tool_call: Optional[dict] = None   # set when the request paused on a tool call
 
 
 @dataclass
@@ -104,6 +106,7 @@ class LLMEngine:
         self.detokenize = True  # incremental text per token (off for token-id-only clients)
         self.spec = None  # speculative decoder (engine/speculative.py) when configured
         self.kv_policy = None  # KV compression policy (kv/compression.py) when configured
+        self.tool_detector = None  # tool-call detection (extras/tools.py) when enabled
         log.info("engine ready: %d KV blocks of %d tokens (%.1f GiB)", nb, cfg.cache.block_size,
                  self.kv.storage.numel() * 2 / 2**30)
         if cfg.cache.h2o_budget > 0:
@@ -175,17 +178,57 @@ class LLMEngine:
     def has_unfinished(self) -> bool:
         return self.scheduler.has_work()
 
+    def has_runnable(self) -> bool:
+        """Work that can make progress (requests paused on a tool call wait for a result)."""
+        return bool(self.scheduler.waiting) or any(
+            s.status != SeqStatus.AWAITING_TOOL for s in self.scheduler.running)
+
+    # ---- tool calls (reference src/engine/tool_call.rs, parallel_model_manager.rs) ----------
+    def enable_tool_calls(self, detector=None):
+        """Pause a request in AWAITING_TOOL (its KV kept) when its generated text contains a
+        complete tool call; :meth:`inject_tool_result` resumes it."""
+        from ..extras.tools import ToolCallDetector
+        self.tool_detector = detector or ToolCallDetector()
+        return self.tool_detector
+
+    def awaiting_tool(self) -> List[Sequence]:
+        return [s for s in self.scheduler.running if s.status == SeqStatus.AWAITING_TOOL]
+
+    def inject_tool_result(self, request_id: str, text: Optional[str] = None,
+                           token_ids: Optional[List[int]] = None) -> Sequence:
+        """Append a tool's result as context after the paused request's output (a mini-prefill
+        into the preserved KV on the next step) and resume generation."""
+        for seq in self.scheduler.running:
+            if seq.request_id == request_id and seq.status == SeqStatus.AWAITING_TOOL:
+                break
+        else:
+            raise KeyError(f"{request_id}: no request awaiting a tool result")
+        ids = list(token_ids) if token_ids is not None else self.tokenizer.encode(
+            text or "", False)
+        if seq.num_tokens + len(ids) >= self.cfg.scheduler.max_model_len:
+            raise ValueError("tool result does not fit in the context")
+        seq.append_context(ids)
+        seq.pending_tool_call = None
+        seq.status = SeqStatus.RUNNING
+        return seq
+
     # ---------------------------------------------------------------------------------
     def step(self) -> List[RequestOutput]:
-        if self.spec is not None and self.spec.active:
-            return self.spec.step(self)
-        so = self.scheduler.schedule()
-        if so.empty:
-            return []
-        if self.kv_policy is not None and hasattr(self.kv_policy, "before_step"):
-            self.kv_policy.before_step(so)
-        res = self.runner.execute(so)
-        return self._process(res.chunks, res.tokens)
+        with trace.nvtx_range("engine.step"):
+            if self.spec is not None and self.spec.active:
+                return self.spec.step(self)
+            with trace.nvtx_range("schedule"):
+                so = self.scheduler.schedule()
+            if so.empty:
+                return []
+            if trace.enabled("scheduler"):
+                trace.debug("scheduler", "step: %d decode, %d prefill chunks, %d tokens",
+                            len(so.decode), len(so.prefill), so.num_tokens)
+            if self.kv_policy is not None and hasattr(self.kv_policy, "before_step"):
+                self.kv_policy.before_step(so)
+            with trace.nvtx_range("execute"):
+                res = self.runner.execute(so)
+            return self._process(res.chunks, res.tokens)
 
     def enable_kv_compression(self, kind: str = "h2o", budget: int = 2048, sinks: int = 4,
                               **kw):
@@ -246,11 +289,19 @@ class LLMEngine:
             reason = "length"
         elif seq.num_tokens >= self.cfg.scheduler.max_model_len:
             reason = "length"
+        call = None
+        if reason is None and self.tool_detector is not None and seq.output_text:
+            call = self.tool_detector.find(seq.output_text[seq.tool_scan_from:])
+            if call is not None:
+                seq.tool_scan_from = len(seq.output_text)
+                seq.pending_tool_call = call
+                seq.status = SeqStatus.AWAITING_TOOL
         if reason is not None:
             self.scheduler.finish(seq, reason)
             self.stats.finished += 1
         return RequestOutput(seq.request_id, [tok], delta, reason is not None, reason,
-                             seq.prompt_len, len(seq.output_token_ids), seq.num_cached_prefix)
+                             seq.prompt_len, len(seq.output_token_ids), seq.num_cached_prefix,
+                             call)
 
     # ---------------------------------------------------------------------------------
     def generate(self, prompts: Union[str, List[str], None] = None,
@@ -265,7 +316,7 @@ class LLMEngine:
         else:
             for p in prompts or []:
                 seqs.append(self.add_request(prompt=p, params=params))
-        while any(not s.finished for s in seqs):
+        while any(not s.finished for s in seqs) and self.has_runnable():
             self.step()
         return seqs
 

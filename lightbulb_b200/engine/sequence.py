@@ -48,6 +48,10 @@ class Sequence:
     evicted: int = 0                 # tokens dropped from the KV cache (compression)
     # speculative decoding
     spec_draft_tokens: List[int] = field(default_factory=list)
+    # tool calls: the pending call while AWAITING_TOOL, context tokens injected afterwards
+    pending_tool_call: Optional[dict] = None
+    injected_tokens: int = 0
+    tool_scan_from: int = 0          # output_text offset already scanned for tool calls
 
     def __post_init__(self) -> None:
         # prompt + generated ids in one list, appended in place (never rebuilt per step)
@@ -58,9 +62,18 @@ class Sequence:
         self._tokens.append(tok)
 
     def truncate_output(self, n: int) -> None:
-        """Keep the first ``n`` generated tokens (speculative rollback)."""
-        del self.output_token_ids[n:]
-        del self._tokens[len(self.prompt_token_ids) + n:]
+        """Keep the first ``n`` generated tokens (speculative rollback of the newest outputs,
+        which are always at the end of the token list)."""
+        k = len(self.output_token_ids) - n
+        if k > 0:
+            del self.output_token_ids[n:]
+            del self._tokens[len(self._tokens) - k:]
+
+    def append_context(self, ids: List[int]) -> None:
+        """Context tokens that are not model outputs (a tool's result): fed through the model
+        as a mini-prefill into the preserved KV, never counted as generated tokens."""
+        self._tokens.extend(ids)
+        self.injected_tokens += len(ids)
 
     @property
     def all_token_ids(self) -> List[int]:

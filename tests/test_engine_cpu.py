@@ -105,3 +105,43 @@ def test_padded_head_widths_match_oracle(hidden, heads, kv):
     sp = SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True)
     for p, s in zip(prompts, eng.generate(prompt_token_ids=prompts, params=sp)):
         assert_greedy_consistent(ref, p, s.output_token_ids)
+
+
+def test_tool_call_pause_and_inject_resumes_in_place():
+    from lightbulb_b200.engine.sequence import SeqStatus
+    cfg, w, eng = _engine()
+    ref = ReferenceLlama(cfg, w)
+
+    class AfterThreeChars:   # stands in for a <tool_call>...</tool_call> match
+        def __init__(self):
+            self.fired = False
+
+        def find(self, text):
+            if not self.fired and len(text) >= 3:
+                self.fired = True
+                return {"raw": "lookup", "call": {"name": "lookup"}}
+            return None
+
+    eng.enable_tool_calls(AfterThreeChars())
+    sp = SamplingParams(temperature=0.0, max_tokens=10, ignore_eos=True, detokenize=True)
+    seq = eng.add_request("t", prompt_token_ids=list(range(5, 40)), params=sp)
+    outs = []
+    while eng.has_runnable():
+        outs += eng.step()
+    assert seq.status == SeqStatus.AWAITING_TOOL and seq.pending_tool_call["raw"] == "lookup"
+    assert any(o.tool_call is not None for o in outs)
+    n_before = len(seq.output_token_ids)
+    assert 0 < n_before < 10 and eng.step() == []          # paused: nothing to run
+    eng.inject_tool_result("t", token_ids=[300, 301, 302, 303])
+    while eng.has_unfinished():
+        eng.step()
+    assert len(seq.output_token_ids) == 10 and seq.injected_tokens == 4
+    toks = seq.all_token_ids
+    assert toks[35 + n_before:35 + n_before + 4] == [300, 301, 302, 303]
+    # every output after the injection follows the oracle on the full token list
+    ref.reset()
+    lg = ref.forward(torch.tensor(toks[:-1]))
+    for j in range(35 + n_before + 4, len(toks)):
+        v, ix = torch.topk(lg[j - 1], 2)
+        assert int(ix[0]) == toks[j] or (v[0] - v[1]) < 0.02
+    assert eng.blocks.check_invariants()

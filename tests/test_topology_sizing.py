@@ -108,3 +108,14 @@ def test_profile_and_auto_detect_with_fake_topology():
     assert sizing.recommend_model(prof, seq_len=4096, min_batch=32) == "llama3-8b"
     sc = sizing.SystemConfig.auto_detect(seq_len=4096, model="llama3-8b", topology=topo)
     assert sc.model == "llama3-8b" and sc.batch_size > 100 and sc.plan.fits
+
+
+def test_trace_categories_and_nvtx_noop():
+    from lightbulb_b200.utils import trace
+    trace.configure(debug="kv,spec", nvtx=False)
+    assert trace.enabled("kv") and trace.enabled("spec") and not trace.enabled("decode")
+    with trace.nvtx_range("x"):
+        trace.debug("kv", "message %d", 1)
+    trace.configure(debug="all", nvtx=False)
+    assert all(trace.enabled(c) for c in trace.CATEGORIES)
+    trace.configure(debug="", nvtx=False)
