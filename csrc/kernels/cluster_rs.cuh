@@ -14,10 +14,10 @@
 //            for peers cannot deadlock;
 //   fetch    one thread per owner bulk-loads, from every peer, that peer's slots of the owned
 //            chunks (one copy per peer, completion on an mbarrier);
-//   reduce   owners sum the S slots in rank order (deterministic), format the output in shared
-//            memory (bf16 + residual, SwiGLU, or fp32) and one thread writes it with 2-D TMA
-//            stores (one store for all owned chunks when S divides the chunk count; the tensor
-//            map clips the M / N edges).
+//   reduce   each epilogue warp takes its own owned chunks (no CTA barrier): sums the S slots in
+//            rank order (deterministic), formats the chunk's output in its first slot (bf16 +
+//            residual, SwiGLU, or fp32) and writes it with a 2-D TMA store (the tensor map clips
+//            the M / N edges).
 //
 // Measured on B200: per-thread global stores from these CTAs drained at a few GB/s per SM,
 // distributed shared memory moved 128 KB partials at ~6-15 GB/s per SM, and every bulk / TMA
@@ -25,9 +25,8 @@
 //
 // Shared layout: slots [S * own][16 columns][128 rows] fp32 (8 KB each).  Slot c holds this
 // CTA's chunk c while publishing; after the barrier, slot s * own + oc holds source s's part of
-// owned chunk r * own + oc (the own part, s = r, is already in place).  Output tile of owned
-// chunk oc: bytes [oc * T, (oc + 1) * T) from the start of the slots, T = 16 x box width x
-// element size <= 8 KB, written only after every thread has read slots 0 .. oc.
+// owned chunk r * own + oc (the own part, s = r, is already in place).  The output tile of owned
+// chunk oc overwrites slot oc (its source-0 part) once the owning warp has read it.
 #pragma once
 
 #include "common.cuh"
@@ -51,10 +50,8 @@ __host__ __device__ constexpr int owned_chunks(int bt, int rank, int S) {
 __host__ __device__ constexpr int num_slots(int bt, int S) { return S * own_max(bt, S); }
 // Shared memory the exchange and the output staging need (reuses the drained pipeline).
 __host__ __device__ constexpr int smem_bytes(int bt, int S) { return num_slots(bt, S) * SLOT_BYTES; }
-// Rows of one output TMA box: all owned chunks at once when every rank owns the same count.
-__host__ __device__ constexpr int out_box_rows(int bt, int S) {
-  return num_chunks(bt) % S == 0 ? CW * own_max(bt, S) : CW;
-}
+// Rows of one output TMA box (one chunk).
+__host__ __device__ constexpr int out_box_rows(int bt, int S) { return CW; }
 // Global workspace floats for `tiles` output tiles split S ways.
 __host__ __device__ constexpr long long ws_floats(int tiles, int bt, int S) {
   return static_cast<long long>(tiles) * S * bt * 128;
@@ -87,14 +84,15 @@ __device__ __forceinline__ void publish(uint32_t tbase, bool have_acc, float* sl
                                         float* ws_tile, uint32_t rank, uint32_t S, int row,
                                         int e, unsigned long long* tr = nullptr) {
   constexpr int NC = num_chunks(BT);
-  constexpr int PER = NC >= 4 ? 4 : NC;  // chunks per TMEM round trip
+  constexpr int PER = NC >= 8 ? 8 : NC >= 4 ? 4 : NC;  // chunks per TMEM round trip
 #pragma unroll 1
   for (int c0 = 0; c0 < NC; c0 += PER) {
     uint32_t r[16 * PER];
     if (have_acc) {
-      if constexpr (PER == 4) {
-        tmem_ld32(tbase + c0 * CW, *reinterpret_cast<uint32_t(*)[32]>(r));
-        tmem_ld32(tbase + c0 * CW + 32, *reinterpret_cast<uint32_t(*)[32]>(r + 32));
+      if constexpr (PER >= 4) {
+#pragma unroll
+        for (int h = 0; h < PER / 2; ++h)
+          tmem_ld32(tbase + c0 * CW + 32 * h, *reinterpret_cast<uint32_t(*)[32]>(r + 32 * h));
       } else if constexpr (PER == 2) {
         tmem_ld32(tbase + c0 * CW, *reinterpret_cast<uint32_t(*)[32]>(r));
       } else {
@@ -151,45 +149,41 @@ __device__ __forceinline__ void fetch(float* slots, float* ws_tile, uint64_t* rb
                 n_own * SLOT_BYTES, rbar);
 }
 
-// All 128 epilogue threads: wait for the fetched slots, then for each owned chunk thread e
-// sums weight rows 4 (e & 31) .. +3 of token columns (e >> 5) + 4 q (q < 4) over the S sources
-// in rank order and, once every thread has read the chunk's slots (named barrier 1), calls
-// epi(oc, first token column of the chunk, e >> 5, e & 31, acc[4]); epi may then write the
-// output tile of chunk oc.  Returns false if the fetch did not complete in time.
+// All 128 epilogue threads: wait for the fetched slots; epilogue warp w (= e >> 5) reduces the
+// owned chunks oc with oc % 4 == w on its own (no CTA barrier): lane l sums weight rows
+// 4 l .. +3 of the chunk's 16 token columns over the S sources in rank order, then calls
+// epi(oc, first token column of the chunk, lane, acc[16]) with acc[j] = rows 4 l .. +3 of
+// column j.  epi may overwrite the chunk's first slot (only this warp reads it).  Returns false
+// if the fetch did not complete in time.
 template <int BT, class Epi>
 __device__ __forceinline__ bool reduce(const float* slots, uint64_t* rbar, uint32_t rank,
-                                       uint32_t S, int e, volatile int* abort_flag, Epi&& epi,
-                                       unsigned long long* tr = nullptr) {
+                                       uint32_t S, int e, volatile int* abort_flag, Epi&& epi) {
   const int n_own = owned_chunks(BT, rank, S);
   if (n_own == 0) return true;
   const int own = own_max(BT, S);
   const bool ok = S == 1 || mbar_wait(rbar, 0, abort_flag);
-  if (tr && e == 0) tr[4] = globaltimer_ns();
-  const int ew = e >> 5, el = e & 31;
+  const int w = e >> 5, l = e & 31;
 #pragma unroll 1
-  for (int oc = 0; oc < n_own; ++oc) {
-    float4 acc[4];
+  for (int oc = w; oc < n_own; oc += 4) {
+    float4 acc[CW];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < CW; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
     if (ok) {
       for (uint32_t s = 0; s < S; ++s) {
-        const float* slot = slots + (s * own + oc) * SLOT_FLOATS + 4 * el;
-        float4 v[4];
+        const float* slot = slots + (s * own + oc) * SLOT_FLOATS + 4 * l;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) v[q] = *reinterpret_cast<const float4*>(slot + (ew + 4 * q) * 128);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          acc[q].x += v[q].x;
-          acc[q].y += v[q].y;
-          acc[q].z += v[q].z;
-          acc[q].w += v[q].w;
+        for (int j = 0; j < CW; ++j) {
+          const float4 v = *reinterpret_cast<const float4*>(slot + j * 128);
+          acc[j].x += v.x;
+          acc[j].y += v.y;
+          acc[j].z += v.z;
+          acc[j].w += v.w;
         }
       }
     }
-    named_bar_sync(1, 128);  // slots 0 .. oc are read: chunk oc's output tile may be written
-    epi(oc, (rank * own + oc) * CW, ew, el, acc);
+    __syncwarp();  // every lane has read the chunk's slots before any lane overwrites them
+    epi(oc, (rank * own + oc) * CW, l, acc);
   }
-  if (tr && e == 0) tr[5] = globaltimer_ns();
   return ok;
 }
 
@@ -198,79 +192,70 @@ __device__ __forceinline__ float silu_c(float x) { return x / (1.0f + __expf(-x)
 // Output modes of stage_out / the tile tensor map.
 enum OutMode : int { kOutBf16 = 0, kOutSwiGLU = 1, kOutF32 = 2 };
 
-__host__ __device__ constexpr int out_tile_bytes(int mode) {
-  return mode == kOutSwiGLU ? CW * 64 * 2 : mode == kOutF32 ? CW * 128 * 4 : CW * 128 * 2;
-}
-__device__ __forceinline__ uint8_t* out_tile(float* slots, int mode, int oc) {
-  return reinterpret_cast<uint8_t*>(slots) + oc * out_tile_bytes(mode);
+// Output staging tile of owned chunk oc: its first slot (16 tokens x box width, <= 8 KB).
+__device__ __forceinline__ uint8_t* out_tile(float* slots, uint32_t own, int oc) {
+  return reinterpret_cast<uint8_t*>(slots + oc * SLOT_FLOATS);
 }
 
 // Format one reduced chunk into its staging tile (row-major [16 tokens][box width], the layout
-// of the 2-D TMA store box).  Thread (ew, el) holds rows 4 el .. +3 of token columns ew + 4 q.
+// of the 2-D TMA store box).  Lane l holds rows 4 l .. +3 of every token column j (acc[j]).
 // res (optional, bf16 mode): residual at (first token of the chunk, first row of the tile);
 // rows_left / cols_left bound the residual reads.
-__device__ __forceinline__ void stage_out(int mode, uint8_t* out, int ew, int el,
-                                          float4 (&acc)[4], const bf16* res, int ldr,
-                                          int rows_left, int cols_left) {
+__device__ __forceinline__ void stage_out(int mode, uint8_t* out, int l, float4 (&acc)[CW],
+                                          const bf16* res, int ldr, int rows_left,
+                                          int cols_left) {
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const int j = ew + 4 * q;
+  for (int j = 0; j < CW; ++j) {
     if (mode == kOutSwiGLU) {
       // lanes 0..15 hold gate rows 0..63, lanes 16..31 the up rows of the same features
       float4 up;
-      up.x = __shfl_down_sync(0xffffffffu, acc[q].x, 16);
-      up.y = __shfl_down_sync(0xffffffffu, acc[q].y, 16);
-      up.z = __shfl_down_sync(0xffffffffu, acc[q].z, 16);
-      up.w = __shfl_down_sync(0xffffffffu, acc[q].w, 16);
-      if (el < 16) {
+      up.x = __shfl_down_sync(0xffffffffu, acc[j].x, 16);
+      up.y = __shfl_down_sync(0xffffffffu, acc[j].y, 16);
+      up.z = __shfl_down_sync(0xffffffffu, acc[j].z, 16);
+      up.w = __shfl_down_sync(0xffffffffu, acc[j].w, 16);
+      if (l < 16) {
         uint2 pk;
-        pk.x = pack_bf16x2(silu_c(acc[q].x) * up.x, silu_c(acc[q].y) * up.y);
-        pk.y = pack_bf16x2(silu_c(acc[q].z) * up.z, silu_c(acc[q].w) * up.w);
-        *reinterpret_cast<uint2*>(out + (j * 64 + 4 * el) * 2) = pk;
+        pk.x = pack_bf16x2(silu_c(acc[j].x) * up.x, silu_c(acc[j].y) * up.y);
+        pk.y = pack_bf16x2(silu_c(acc[j].z) * up.z, silu_c(acc[j].w) * up.w);
+        *reinterpret_cast<uint2*>(out + (j * 64 + 4 * l) * 2) = pk;
       }
     } else if (mode == kOutF32) {
-      *reinterpret_cast<float4*>(out + (j * 128 + 4 * el) * 4) = acc[q];
+      *reinterpret_cast<float4*>(out + (j * 128 + 4 * l) * 4) = acc[j];
     } else {
-      float v[4] = {acc[q].x, acc[q].y, acc[q].z, acc[q].w};
+      float v[4] = {acc[j].x, acc[j].y, acc[j].z, acc[j].w};
       if (res != nullptr && j < rows_left) {
-        const bf16* rr = res + static_cast<size_t>(j) * ldr + 4 * el;
+        const bf16* rr = res + static_cast<size_t>(j) * ldr + 4 * l;
 #pragma unroll
         for (int u = 0; u < 4; ++u)
-          if (4 * el + u < cols_left) v[u] += __bfloat162float(rr[u]);
+          if (4 * l + u < cols_left) v[u] += __bfloat162float(rr[u]);
       }
       uint2 pk;
       pk.x = pack_bf16x2(v[0], v[1]);
       pk.y = pack_bf16x2(v[2], v[3]);
-      *reinterpret_cast<uint2*>(out + (j * 128 + 4 * el) * 2) = pk;
+      *reinterpret_cast<uint2*>(out + (j * 128 + 4 * l) * 2) = pk;
     }
   }
 }
 
-// After every owned chunk is staged (all 128 threads): one thread stores the tiles.  x0 = first
-// output column of the tile in the tensor map's units, m0 = first token of the tile.  The
-// tensor map's box is out_box_rows(BT, S) rows high.  wait_all: wait until the writes are
-// performed (a completion signal follows), else only until shared memory may be released.
-template <int BT>
-__device__ __forceinline__ void store_out(const CUtensorMap* tmap, float* slots, int mode, int e,
-                                          uint32_t rank, uint32_t S, int x0, int m0,
-                                          bool wait_all, unsigned long long* tr = nullptr) {
+// Right after stage_out of chunk oc (all 32 lanes of the owning warp): lane 0 writes the tile
+// with a 2-D TMA store at (x0, first token of the chunk).
+__device__ __forceinline__ void store_chunk(const CUtensorMap* tmap, const uint8_t* tile, int l,
+                                            int x0, int y0) {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  named_bar_sync(1, 128);
-  if (e != 0) return;
-  if (tr) tr[6] = globaltimer_ns();
-  const int n_own = owned_chunks(BT, rank, S);
-  if (n_own == 0) return;
-  const int first = m0 + rank * own_max(BT, S) * CW;
-  if (out_box_rows(BT, S) > CW) {
-    tma_store_2d(tmap, out_tile(slots, mode, 0), x0, first);
-  } else {
-    for (int oc = 0; oc < n_own; ++oc)
-      tma_store_2d(tmap, out_tile(slots, mode, oc), x0, first + oc * CW);
+  __syncwarp();
+  if (l == 0) {
+    tma_store_2d(tmap, tile, x0, y0);
+    bulk_commit();
   }
-  bulk_commit();
-  if (wait_all) bulk_wait_all0();
-  else bulk_wait_read0();
-  if (tr) tr[7] = globaltimer_ns();
+}
+
+// After a warp's last store_chunk: lane 0 waits until its stores have read shared memory
+// (wait_all: until the writes are performed, when a completion signal follows).
+__device__ __forceinline__ void store_wait(int l, bool wait_all) {
+  if (l == 0) {
+    if (wait_all) bulk_wait_all0();
+    else bulk_wait_read0();
+  }
 }
 
 }  // namespace crs

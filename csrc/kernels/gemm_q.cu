@@ -279,12 +279,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int e = threadIdx.x - 64;
     if (e == 0) crs::fetch<BT>(sSlots, ws_tile, rbar, rank, S);
     const int m0 = mt * BT;
-    auto epi = [&](int oc, int t0, int ew, int el, float4 (&acc)[4]) {
-      crs::stage_out(a.mode, crs::out_tile(sSlots, a.mode, oc), ew, el, acc, nullptr, 0, 0, 0);
+    const int x0 = a.mode == 1 ? nt * 64 : nt * BW;
+    auto epi = [&](int oc, int t0, int l, float4 (&acc)[crs::CW]) {
+      uint8_t* tile = crs::out_tile(sSlots, 0, oc);
+      crs::stage_out(a.mode, tile, l, acc, nullptr, 0, 0, 0);
+      crs::store_chunk(&tmC, tile, l, x0, m0 + t0);
     };
     const bool ok = crs::reduce<BT>(sSlots, rbar, rank, S, e, abort_flag, epi);
-    crs::store_out<BT>(&tmC, sSlots, a.mode, e, rank, S, a.mode == 1 ? nt * 64 : nt * BW, m0,
-                       false);
+    crs::store_wait(e & 31, false);
     if (!ok) {
       record_error(a.err, kErrTimeoutTmaFull);
       *abort_flag = 1;

@@ -609,40 +609,42 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int omode = a.mode == kEpiSwiGLU ? crs::kOutSwiGLU
                       : a.mode == kEpiF32  ? crs::kOutF32
                                            : crs::kOutBf16;
-    // thread: weight rows 4 el .. +3, token columns t0 + ew + 4 q
-    auto epi = [&](int oc, int t0, int ew, int el, float4 (&acc)[4]) {
+    const int x0 = omode == crs::kOutSwiGLU ? nt * 64 : nt * BW;
+    // lane l: weight rows 4 l .. +3 of the chunk's token columns t0 .. t0 + 15 (acc[j])
+    auto epi = [&](int oc, int t0, int l, float4 (&acc)[crs::CW]) {
       if (a.tma_out) {
         const int mf = m0 + t0, n0 = nt * BW;
         const bf16* res = a.residual != nullptr
                               ? a.residual + static_cast<size_t>(mf) * a.ldr + n0
                               : nullptr;
-        crs::stage_out(omode, crs::out_tile(sSlots, omode, oc), ew, el, acc, res, a.ldr,
-                       a.M - mf, a.N - n0);
+        uint8_t* tile = crs::out_tile(sSlots, 0, oc);
+        crs::stage_out(omode, tile, l, acc, res, a.ldr, a.M - mf, a.N - n0);
+        crs::store_chunk(&tmC, tile, l, x0, mf);
         return;
       }
       // per-thread stores (tensor-parallel scatter into peers' slots, or unaligned C)
-      const int r0 = 4 * el;
+      const int r0 = 4 * l;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int m = m0 + t0 + ew + 4 * q;
+      for (int j = 0; j < crs::CW; ++j) {
+        const int m = m0 + t0 + j;
         if (a.mode == kEpiSwiGLU) {
           float4 up;
-          up.x = __shfl_down_sync(0xffffffffu, acc[q].x, 16);
-          up.y = __shfl_down_sync(0xffffffffu, acc[q].y, 16);
-          up.z = __shfl_down_sync(0xffffffffu, acc[q].z, 16);
-          up.w = __shfl_down_sync(0xffffffffu, acc[q].w, 16);
+          up.x = __shfl_down_sync(0xffffffffu, acc[j].x, 16);
+          up.y = __shfl_down_sync(0xffffffffu, acc[j].y, 16);
+          up.z = __shfl_down_sync(0xffffffffu, acc[j].z, 16);
+          up.w = __shfl_down_sync(0xffffffffu, acc[j].w, 16);
           const int f = nt * 64 + r0;
-          if (el < 16 && m < a.M && f < (a.N >> 1)) {
+          if (l < 16 && m < a.M && f < (a.N >> 1)) {
             uint2 pk;
-            pk.x = pack_bf16x2(silu(acc[q].x) * up.x, silu(acc[q].y) * up.y);
-            pk.y = pack_bf16x2(silu(acc[q].z) * up.z, silu(acc[q].w) * up.w);
+            pk.x = pack_bf16x2(silu(acc[j].x) * up.x, silu(acc[j].y) * up.y);
+            pk.y = pack_bf16x2(silu(acc[j].z) * up.z, silu(acc[j].w) * up.w);
             *reinterpret_cast<uint2*>(out_row(a, m) + f) = pk;
           }
           continue;
         }
         const int n = nt * BW + r0;
         if (m >= a.M || n >= a.N) continue;
-        float vv[4] = {acc[q].x, acc[q].y, acc[q].z, acc[q].w};
+        float vv[4] = {acc[j].x, acc[j].y, acc[j].z, acc[j].w};
         if (a.mode == kEpiF32) {
           float* C = reinterpret_cast<float*>(a.C) + static_cast<size_t>(m) * a.ldc;
 #pragma unroll
@@ -669,11 +671,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     };
-    unsigned long long* tr2 = tr ? a.trace + (gridDim.x + blockIdx.x) * 8 : nullptr;
-    const bool ok = crs::reduce<BT>(sSlots, rbar, rank, S, e, abort_flag, epi, tr2);
-    if (a.tma_out)
-      crs::store_out<BT>(&tmC, sSlots, omode, e, rank, S, omode == crs::kOutSwiGLU ? nt * 64 : nt * BW,
-                         m0, a.tp.done_counter != nullptr, tr2);
+    const bool ok = crs::reduce<BT>(sSlots, rbar, rank, S, e, abort_flag, epi);
+    if (a.tma_out) crs::store_wait(e & 31, a.tp.done_counter != nullptr);
     if (!ok) {
       record_error(a.err, kErrTimeoutTmaFull);
       *abort_flag = 1;
