@@ -113,9 +113,20 @@ class ClockSampler:
         except Exception:
             self.proc = None
 
+    def _count(self) -> int:
+        try:
+            with open(self.path) as f:
+                return sum(1 for ln in f if not self.uuid or self.uuid in ln)
+        except OSError:
+            return 0
+
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        # a short timed region can end before the sampler's first line: wait for one
+        t0 = time.time()
+        while self._count() == 0 and time.time() - t0 < 1.0:
+            time.sleep(0.05)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -137,6 +148,22 @@ class ClockSampler:
                 for n, v in zip(names, p[6:10]):
                     if v.lower().startswith("active"):
                         reasons.add(n)
+        if not sm:
+            # one synchronous query as the last resort
+            try:
+                out = subprocess.run(["nvidia-smi", f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True,
+                                     text=True, timeout=10).stdout
+                for line in out.splitlines():
+                    p = [x.strip() for x in line.split(",")]
+                    if len(p) >= 10 and (not self.uuid or p[1] == self.uuid):
+                        sm.append(float(p[2]))
+                        mx = float(p[3])
+                        for n, v in zip(names, p[6:10]):
+                            if v.lower().startswith("active"):
+                                reasons.add(n)
+            except Exception:
+                pass
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
                 "reasons": sorted(reasons), "samples": len(sm)}
 
@@ -215,7 +242,16 @@ def bench_decode(args):
     prefill_s = time.perf_counter() - t_arr
     ttfts = sorted(s.first_token_time - s.arrival_time for s in seqs)
 
-    # ---- phase 2: warm-up decode steps ----
+    # ---- phase 2: warm-up decode steps (the clock sampler starts here: same kind of steps,
+    # so a short timed region still has samples under load) ----
+    uuid = ""
+    try:
+        uuid = str(torch.cuda.get_device_properties(local).uuid)
+        uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+    except Exception:
+        pass
+    clocks = ClockSampler(uuid)
+    clocks.start()
     for _ in range(args.warmup):
         eng.step()
     ops.check_errors(dev)
@@ -225,14 +261,6 @@ def bench_decode(args):
     if comm is not None:
         comm.barrier()
     torch.cuda.synchronize()
-    uuid = ""
-    try:
-        uuid = str(torch.cuda.get_device_properties(local).uuid)
-        uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
-    except Exception:
-        pass
-    clocks = ClockSampler(uuid)
-    clocks.start()
     ev = eng.runner.enable_step_events()
     ops.launch_counter_reset()
     tokens = 0

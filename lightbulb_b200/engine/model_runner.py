@@ -38,9 +38,10 @@ class StepResult:
 
 
 class _GraphBucket:
-    def __init__(self, runner: "ModelRunner", bsz: int):
+    def __init__(self, runner: "ModelRunner", bsz: int, greedy: bool = False):
         r = runner
         self.bsz = bsz
+        self.greedy = greedy   # tensor parallel: every row greedy -> argmax without full logits
         dev = r.device
         W = r.max_blocks_per_seq
         self.W = W
@@ -75,8 +76,11 @@ class _GraphBucket:
 
     def run(self, runner: "ModelRunner"):
         logits = runner.model.forward(self.batch(), runner.kv)
-        runner.postprocess_logits(logits, self.temp, self.top_k, self.top_p, self.seeds,
-                                  self.out_tokens)
+        if self.greedy:
+            runner.comm.argmax_vocab_parallel(logits, self.out_tokens)
+        else:
+            runner.postprocess_logits(logits, self.temp, self.top_k, self.top_p, self.seeds,
+                                      self.out_tokens)
 
 
 class ModelRunner:
@@ -153,9 +157,13 @@ class ModelRunner:
         torch.cuda.synchronize() if self.is_cuda else None
 
     # -------------------------------------------------------------------------------
-    def postprocess_logits(self, logits, temp, top_k, top_p, seeds, out_tokens):
+    def postprocess_logits(self, logits, temp, top_k, top_p, seeds, out_tokens,
+                           greedy: bool = False):
         if self.comm is not None and self.comm.world > 1:
-            self.comm.sample_vocab_parallel(logits, temp, top_k, top_p, seeds, out_tokens)
+            if greedy:
+                self.comm.argmax_vocab_parallel(logits, out_tokens)
+            else:
+                self.comm.sample_vocab_parallel(logits, temp, top_k, top_p, seeds, out_tokens)
         else:
             ops.sample(logits, temp, top_k, top_p, seeds, out_tokens)
 
@@ -195,12 +203,19 @@ class ModelRunner:
     def _fill_block_tables(self, seqs, out_np: np.ndarray, width: int):
         self.bm.fill_block_tables([s.seq_id for s in seqs], out_np, width)
 
+    def _greedy_variant(self, chunks) -> bool:
+        """Tensor parallel only: a batch of greedy rows replays the graph whose sampling tail
+        all-gathers (max, index) pairs instead of the full vocab-parallel logits."""
+        return (self.comm is not None and self.comm.world > 1 and
+                all(c.seq.params.temperature <= 0 for c in chunks))
+
     def _run_graph(self, chunks: List[ScheduledChunk]) -> List[int]:
         B = len(chunks)
         bsz = self.buckets[bisect.bisect_left(self.buckets, B)]
-        g = self.graphs.get(bsz)
+        greedy = self._greedy_variant(chunks)
+        g = self.graphs.get((bsz, greedy))
         if g is None:
-            g = self._capture(bsz)
+            g = self._capture(bsz, greedy)
         W = g.W
         hi = self.h_ints[:g.n_int].numpy()
         hi[:] = 0
@@ -240,8 +255,8 @@ class ModelRunner:
         self.d2h_bytes = bsz * 4
         return out[:B].tolist()
 
-    def _capture(self, bsz: int) -> _GraphBucket:
-        g = _GraphBucket(self, bsz)
+    def _capture(self, bsz: int, greedy: bool = False) -> _GraphBucket:
+        g = _GraphBucket(self, bsz, greedy)
         # valid dummy inputs: every row points at block 0 with one token, no KV write
         g.cu_q.copy_(torch.arange(bsz + 1, dtype=torch.int32))
         g.seq_lens.fill_(1)
@@ -264,14 +279,16 @@ class ModelRunner:
         ops.launch_counter_add(-g.launches)  # capture launched nothing
         torch.cuda.synchronize()
         g.graph = graph
-        self.graphs[bsz] = g
+        self.graphs[(bsz, greedy)] = g
         return g
 
     def capture_all(self, up_to: Optional[int] = None) -> None:
+        tp = self.comm is not None and self.comm.world > 1
         for b in self.buckets:
             if up_to is None or b <= up_to:
-                if b not in self.graphs:
-                    self._capture(b)
+                for greedy in ((False, True) if tp else (False,)):
+                    if (b, greedy) not in self.graphs:
+                        self._capture(b, greedy)
 
     def _run_eager(self, chunks: List[ScheduledChunk], num_decode: int) -> List[int]:
         B = len(chunks)
@@ -357,7 +374,9 @@ class ModelRunner:
         ev = self._ev_start() if self.is_cuda else None
         logits = self.model.forward(fb, self.kv)
         out = torch.empty(nlog, dtype=torch.int32, device=self.device)
-        self.postprocess_logits(logits, df[:nlog], d_top_k, df[nlog:2 * nlog], ds, out)
+        self.postprocess_logits(logits, df[:nlog], d_top_k, df[nlog:2 * nlog], ds, out,
+                                greedy=self._greedy_variant([c for c in chunks
+                                                              if c.needs_logits]))
         self._ev_end(ev)
         if self.is_cuda:
             h = self.h_out[:nlog]

@@ -76,6 +76,24 @@ class TPComm:
         if self.world > 1:
             dist.barrier(group=self.group)
 
+    def argmax_vocab_parallel(self, logits: torch.Tensor, out_tokens: torch.Tensor) -> None:
+        """Greedy over vocab-parallel shards: each rank takes the first maximum of its shard,
+        the ranks all-gather (value, global index) pairs and every rank picks the largest value
+        (ties: the lowest rank, i.e. the smallest global index -- first maximum overall)."""
+        b, vl = logits.shape
+        zeros = torch.zeros(b, dtype=torch.float32, device=logits.device)
+        zi = torch.zeros(b, dtype=torch.int32, device=logits.device)
+        seeds = torch.zeros(b, dtype=torch.int64, device=logits.device)
+        local = torch.empty(b, dtype=torch.int32, device=logits.device)
+        ops.sample(logits, zeros, zi, zeros + 1.0, seeds, local)
+        val = logits.gather(1, local.long()[:, None])[:, 0]
+        pair = torch.stack([val, (local + self.rank * vl).float()], 1).contiguous()  # [b, 2]
+        allp = torch.empty(self.world * b, 2, dtype=torch.float32, device=logits.device)
+        dist.all_gather_into_tensor(allp, pair, group=self.group)
+        allp = allp.view(self.world, b, 2)
+        best = allp[:, :, 0].argmax(0)          # first maximum over ranks (lowest rank on ties)
+        out_tokens.copy_(allp[:, :, 1].gather(0, best[None])[0].to(torch.int32))
+
     def sample_vocab_parallel(self, logits: torch.Tensor, temp: torch.Tensor,
                               top_k: torch.Tensor, top_p: torch.Tensor, seeds: torch.Tensor,
                               out_tokens: torch.Tensor) -> None:

@@ -81,3 +81,41 @@ def test_tp2_matches_single_process():
     # bf16 partial sums reduce in a different order under TP: allow a near-tie flip late on
     for a, b in zip(res[0], ref):
         assert a[:4] == b[:4]
+
+
+def _argmax_worker(rank, world, port, out_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
+    import torch.distributed as dist
+    from datetime import timedelta
+    from lightbulb_b200.parallel.comm import TPComm
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        g = torch.Generator().manual_seed(3)
+        full = torch.randn(5, 40, generator=g)
+        full[1, 7] = full[1, 27] = 9.0        # tie across shards: first (global 7) wins
+        full[2, 30] = 8.0
+        full[3, 12] = full[3, 13] = 7.0       # tie inside a shard
+        shard = full[:, rank * 20:(rank + 1) * 20].contiguous()
+        out = torch.zeros(5, dtype=torch.int32)
+        TPComm().argmax_vocab_parallel(shard, out)
+        out_q.put((rank, out.tolist(), full.argmax(1).tolist()))
+    except Exception as e:
+        out_q.put((rank, f"error: {e!r}", None))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_argmax_vocab_parallel_first_max():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_argmax_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, got, ref in res:
+        assert not isinstance(got, str), got
+        assert got == ref and got[1] == 7 and got[3] == 12
