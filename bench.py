@@ -67,7 +67,8 @@ def parse():
     ap.add_argument("--h2o-sinks", type=int, default=4)
     ap.add_argument("--block-size", type=int, default=16)
     ap.add_argument("--max-batched-tokens", type=int, default=16384)
-    ap.add_argument("--comm", default="nccl", choices=["nccl", "fused"])
+    ap.add_argument("--comm", default="p2p", choices=["nccl", "fused", "p2p"],
+                    help="TP partial-sum collective (engine option parallel.comm)")
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--seed", type=int, default=1234)
     a = ap.parse_args()
@@ -192,7 +193,8 @@ def bench_decode(args):
     import torch.distributed as dist
 
     from lightbulb_b200 import ops
-    from lightbulb_b200.config import (CacheConfig, EngineConfig, SchedulerConfig, get_preset)
+    from lightbulb_b200.config import (CacheConfig, EngineConfig, ParallelConfig, SchedulerConfig,
+                                       get_preset)
     from lightbulb_b200.engine.llm_engine import LLMEngine
     from lightbulb_b200.engine.sampling import SamplingParams
     from lightbulb_b200.models.weights import random_packed_model
@@ -203,9 +205,6 @@ def bench_decode(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     comm = TPComm() if world > 1 else None
-    if comm is not None and args.comm == "fused":
-        from lightbulb_b200.parallel.fused import enable_fused
-        enable_fused(comm)
 
     mcfg = get_preset(args.model)
     out_len = max(args.output_len, args.warmup + args.steps + 2)
@@ -216,7 +215,7 @@ def bench_decode(args):
         scheduler=SchedulerConfig(max_num_seqs=args.requests,
                                   max_num_batched_tokens=args.max_batched_tokens,
                                   chunk_size=args.max_batched_tokens, max_model_len=max_len),
-        use_cuda_graphs=not args.no_graphs)
+        use_cuda_graphs=not args.no_graphs, parallel=ParallelConfig(comm=args.comm))
     t0 = time.perf_counter()
     packed = random_packed_model(mcfg, seed=args.seed, rank=rank, world=world, device=dev)
     torch.cuda.synchronize()
@@ -365,6 +364,8 @@ def _finish(eng, comm):
         spec.draft.release_graphs()
     if comm is not None:
         comm.barrier()
+        comm.close()
+        comm.barrier()
         dist.destroy_process_group()
 
 
@@ -430,7 +431,8 @@ def bench_prefill_prefix(args):
 
     import torch
     from lightbulb_b200 import ops
-    from lightbulb_b200.config import CacheConfig, EngineConfig, SchedulerConfig, get_preset
+    from lightbulb_b200.config import (CacheConfig, EngineConfig, ParallelConfig, SchedulerConfig,
+                                       get_preset)
     from lightbulb_b200.engine.llm_engine import LLMEngine
     from lightbulb_b200.engine.sampling import SamplingParams
     from lightbulb_b200.models.weights import random_packed_model
@@ -443,7 +445,7 @@ def bench_prefill_prefix(args):
                         scheduler=SchedulerConfig(max_num_seqs=args.requests,
                                                   max_num_batched_tokens=args.chunk,
                                                   chunk_size=args.chunk, max_model_len=max_len),
-                        use_cuda_graphs=not args.no_graphs)
+                        use_cuda_graphs=not args.no_graphs, parallel=ParallelConfig(comm=args.comm))
     packed = random_packed_model(mcfg, seed=args.seed, rank=rank, world=world, device=dev)
     eng = LLMEngine(ecfg, packed, None, comm=comm, tp_rank=rank, tp_size=world)
     rng = random.Random(args.seed + 1)
@@ -523,7 +525,8 @@ def bench_prefill_prefix(args):
 def bench_spec(args):
     import torch
     from lightbulb_b200 import ops
-    from lightbulb_b200.config import CacheConfig, EngineConfig, SchedulerConfig, get_preset
+    from lightbulb_b200.config import (CacheConfig, EngineConfig, ParallelConfig, SchedulerConfig,
+                                       get_preset)
     from lightbulb_b200.engine.llm_engine import LLMEngine
     from lightbulb_b200.engine.sampling import SamplingParams
     from lightbulb_b200.models.weights import random_packed_model
@@ -538,7 +541,7 @@ def bench_spec(args):
                                                   max_num_batched_tokens=args.max_batched_tokens,
                                                   chunk_size=args.max_batched_tokens,
                                                   max_model_len=max_len),
-                        use_cuda_graphs=not args.no_graphs)
+                        use_cuda_graphs=not args.no_graphs, parallel=ParallelConfig(comm=args.comm))
     t0 = time.perf_counter()
     packed = random_packed_model(mcfg, seed=args.seed, rank=rank, world=world, device=dev)
     eng = LLMEngine(ecfg, packed, None, comm=comm, tp_rank=rank, tp_size=world)
@@ -608,7 +611,8 @@ def bench_spec(args):
 def bench_awq_h2o(args):
     import torch
     from lightbulb_b200 import ops
-    from lightbulb_b200.config import CacheConfig, EngineConfig, SchedulerConfig, get_preset
+    from lightbulb_b200.config import (CacheConfig, EngineConfig, ParallelConfig, SchedulerConfig,
+                                       get_preset)
     from lightbulb_b200.engine.llm_engine import LLMEngine
     from lightbulb_b200.engine.sampling import SamplingParams
     from lightbulb_b200.models.weights import random_packed_awq_model
@@ -623,7 +627,7 @@ def bench_awq_h2o(args):
                                                   max_num_batched_tokens=args.max_batched_tokens,
                                                   chunk_size=args.max_batched_tokens,
                                                   max_model_len=max_len),
-                        use_cuda_graphs=not args.no_graphs)
+                        use_cuda_graphs=not args.no_graphs, parallel=ParallelConfig(comm=args.comm))
     t0 = time.perf_counter()
     packed = random_packed_awq_model(mcfg, seed=args.seed, rank=rank, world=world, device=dev)
     eng = LLMEngine(ecfg, packed, None, comm=comm, tp_rank=rank, tp_size=world)

@@ -24,6 +24,11 @@ void gemm_bf16_tp(const at::Tensor& A, const at::Tensor& W, at::Tensor& C, int64
                   int64_t slot_stride, int64_t wait_flag_ptr, int64_t wait_count,
                   int64_t done_counter_ptr, int64_t trace_ptr,
                   const c10::optional<at::Tensor>& ws);
+int64_t allreduce_buffer_bytes(int64_t max_elems, int64_t world);
+void allreduce_prepare(int64_t base, int64_t max_elems, int64_t world);
+void allreduce_p2p(at::Tensor& out, const at::Tensor& inp, std::vector<int64_t> bases,
+                   int64_t rank, int64_t n_elems, int64_t max_elems, int64_t ctas,
+                   at::Tensor& err);
 int64_t ipc_alloc(int64_t bytes);
 void ipc_free(int64_t ptr);
 at::Tensor ipc_export(int64_t ptr);
@@ -68,6 +73,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("rows_per_rank"), py::arg("src_rank"), py::arg("slot_stride"),
         py::arg("wait_flag_ptr"), py::arg("wait_count"), py::arg("done_counter_ptr"),
         py::arg("trace_ptr") = 0, py::arg("ws") = py::none());
+  m.def("allreduce_buffer_bytes", &lb::allreduce_buffer_bytes);
+  m.def("allreduce_prepare", &lb::allreduce_prepare);
+  m.def("allreduce_p2p", &lb::allreduce_p2p, "two-shot all-reduce over NVLink peer memory");
   m.def("ipc_alloc", &lb::ipc_alloc);
   m.def("ipc_free", &lb::ipc_free);
   m.def("ipc_export", &lb::ipc_export);

@@ -201,8 +201,11 @@ class SchedulerConfig:
 class ParallelConfig:
     tensor_parallel_size: int = 1
     pipeline_parallel_size: int = 1
-    # "nccl": NCCL collectives only (baseline); "fused": in-kernel NVLink P2P collectives.
-    comm: str = "fused"
+    # Row-parallel partial sums under tensor parallelism:
+    #   "p2p"   one-launch push all-reduce over NVLink peer memory (parallel/allreduce.py);
+    #   "fused" GEMM scatter epilogue + reduce/RMSNorm/all-gather kernel (parallel/fused.py);
+    #   "nccl"  NCCL all_reduce only.
+    comm: str = "p2p"
 
 
 @dataclass

@@ -88,6 +88,8 @@ class LLMEngine:
         if self.tokenizer.eos_token_ids:
             self.eos_ids |= set(self.tokenizer.eos_token_ids)
         max_len = cfg.scheduler.max_model_len
+        if comm is not None and comm.world > 1 and dev.type == "cuda":
+            self._setup_comm(comm, cfg, dev)
         self.model = model or LlamaModel(mcfg, packed_weights, tp_rank, tp_size,
                                          max_positions=max_len + 64, comm=comm)
         nb = derive_num_blocks(mcfg, cfg.cache, tp_size, dev)
@@ -177,6 +179,20 @@ class LLMEngine:
 
     def has_unfinished(self) -> bool:
         return self.scheduler.has_work()
+
+    @staticmethod
+    def _setup_comm(comm, cfg: EngineConfig, dev) -> None:
+        """Enable the configured peer-memory collective before any CUDA graph is captured
+        (every rank takes the same steps: the setup exchanges IPC handles)."""
+        mode = cfg.parallel.comm
+        if mode == "p2p" and comm.p2p_ar is None and not getattr(comm, "fused_requested", False):
+            rows = min(4096, max(cfg.scheduler.max_num_seqs, cfg.scheduler.max_num_batched_tokens))
+            comm.enable_p2p_allreduce(rows * cfg.model.hidden_size, dev)
+        elif mode == "fused" and not getattr(comm, "fused_requested", False):
+            from ..parallel.fused import enable_fused
+            enable_fused(comm)
+        elif mode not in ("p2p", "fused", "nccl"):
+            raise ValueError(f"parallel.comm must be p2p, fused or nccl, not {mode!r}")
 
     def has_runnable(self) -> bool:
         """Work that can make progress (requests paused on a tool call wait for a result)."""

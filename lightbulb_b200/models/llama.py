@@ -196,14 +196,12 @@ class LlamaModel:
                                     cu_q_cpu=b.cu_q_cpu, scale=self.scale)
             if self.h2o is not None and nd > 0 and i == len(self.layers) - 1 and last:
                 self.h2o.accumulate(q[:nd], kv.k[i], b.block_tables[:nd], b.seq_lens[:nd])
-            o = ops.gemm(attn, L["o"])
-            if comm is not None:
-                o = comm.all_reduce(o)
+            o = comm.gemm_all_reduce(attn, L["o"]) if comm is not None else \
+                ops.gemm(attn, L["o"])
             h = ops.rmsnorm(o, L["ln_post"], eps, residual=x)
             act = ops.gemm(h, L["gate_up"], mode=ops.EPI_SWIGLU)
-            dn = ops.gemm(act, L["down"])
-            if comm is not None:
-                dn = comm.all_reduce(dn)
+            dn = comm.gemm_all_reduce(act, L["down"]) if comm is not None else \
+                ops.gemm(act, L["down"])
             if i + 1 < len(self.layers):
                 nw = self.layers[i + 1]["ln_in"]
             elif last:

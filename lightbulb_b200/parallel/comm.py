@@ -48,11 +48,37 @@ class TPComm:
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.fused = None  # set by parallel.fused when peer-memory kernels are enabled
+        self.p2p_ar = None  # two-shot peer-memory all-reduce (parallel/allreduce.py)
 
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         if self.world > 1:
             dist.all_reduce(x, group=self.group)
         return x
+
+    def enable_p2p_allreduce(self, max_elems: int, device=None):
+        """Use the peer-memory all-reduce for partial sums of up to ``max_elems`` elements."""
+        if self.world > 1 and self.p2p_ar is None:
+            from .allreduce import P2PAllReduce
+            dev = device or torch.device("cuda", torch.cuda.current_device())
+            self.p2p_ar = P2PAllReduce(self, max_elems, dev)
+        return self.p2p_ar
+
+    def gemm_all_reduce(self, a: torch.Tensor, w) -> torch.Tensor:
+        """``a @ w.T`` summed over ranks (row-parallel layer): the GEMM writes straight into
+        the peer-visible input of the all-reduce when it fits, else NCCL."""
+        m, n = a.shape[0], w.shape[0]
+        ar = self.p2p_ar
+        if ar is not None and a.is_cuda and ar.fits(m * n):
+            x = ar.input(m, n)
+            ops.gemm(a, w, out=x)
+            return ar(x)
+        return self.all_reduce(ops.gemm(a, w))
+
+    def close(self):
+        if self.p2p_ar is not None:
+            torch.cuda.synchronize()
+            self.p2p_ar.close()
+            self.p2p_ar = None
 
     def min_int(self, v: int) -> int:
         if self.world == 1:

@@ -91,6 +91,24 @@ def main(argv=None) -> int:
         ops.gemm(hh, Wgu, mode=ops.EPI_SWIGLU)
 
     res["nccl_chain_us"] = timed(nccl_chain)
+    # two-shot peer-memory all-reduce (GEMM writes straight into its input)
+    ar = comm.enable_p2p_allreduce(T * H, dev)
+    xin = ar.input(T, H)
+    xin.copy_(o)
+    res["p2p_allreduce_us"] = timed(lambda: ar(xin))
+
+    def p2p_chain():
+        y = comm.gemm_all_reduce(attn, Wo)
+        hh = ops.rmsnorm(y, lnw, 1e-5, residual=x)
+        ops.gemm(hh, Wgu, mode=ops.EPI_SWIGLU)
+
+    res["p2p_chain_us"] = timed(p2p_chain)
+    o2 = ops.gemm(attn, Wo)               # o itself was all-reduced in place by the timing above
+    ref = o2.float().clone()
+    dist.all_reduce(ref)
+    xin.copy_(o2)
+    got = ar(xin).float()
+    res["p2p_max_abs_err_vs_nccl"] = float((got - ref).abs().max())
     F.residual[:R].copy_(x[rank * R:(rank + 1) * R])
 
     def fused_chain():
@@ -131,6 +149,7 @@ def main(argv=None) -> int:
     if rank == 0:
         print(json.dumps({k: (round(v, 2) if isinstance(v, float) else v) for k, v in res.items()}))
     F.close()
+    comm.close()
     comm.barrier()
     dist.destroy_process_group()
     return 0
