@@ -48,6 +48,8 @@ void gemm_quant(const at::Tensor& X, const at::Tensor& qw, const at::Tensor& sca
                 const at::Tensor& offsets, int64_t bits, int64_t group, at::Tensor& C,
                 int64_t mode, int64_t splits, at::Tensor& err, at::Tensor& ws);
 void embedding(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, at::Tensor& err);
+void forward_tokens(at::Tensor& ids, const at::Tensor& src, const at::Tensor& last,
+                    at::Tensor& err);
 void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w,
              at::Tensor& y, double eps);
 void rope_kv(at::Tensor& qkv, const at::Tensor& positions, const c10::optional<at::Tensor>& slots,
@@ -90,6 +92,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kv_compact", &lb::kv_compact, "copy kept KV token slots (all layers)");
   m.def("gemm_quant", &lb::gemm_quant, "dequant-fused tcgen05 GEMM (int4 / int8 groups)");
   m.def("embedding", &lb::embedding, "embedding gather");
+  m.def("forward_tokens", &lb::forward_tokens, "patch input ids from the previous step's samples");
   m.def("rmsnorm", &lb::rmsnorm, "RMSNorm with optional fused residual add");
   m.def("rope_kv", &lb::rope_kv, "RoPE + paged KV append");
   m.def("sample_tokens", &lb::sample_tokens, "greedy / top-k / top-p sampling");

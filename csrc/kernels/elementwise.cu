@@ -16,6 +16,24 @@
 namespace lb {
 
 // ---------------------------------------------------------------------------------------
+// Token forwarding for overlapped decode: ids[i] = last[src[i]] where src[i] >= 0 (the
+// input token of row i is the previous step's sampled token of row src[i], still on the
+// device); rows with src[i] < 0 keep the host-provided id.
+// ---------------------------------------------------------------------------------------
+__global__ void forward_tokens_kernel(int* ids, const int* src, const int* last, int n,
+                                      int last_n, int* err) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int s = src[i];
+  if (s < 0) return;
+  if (s >= last_n) {
+    record_error(err, kErrBounds);
+    return;
+  }
+  ids[i] = last[s];
+}
+
+// ---------------------------------------------------------------------------------------
 // Embedding: out[t, :] = table[ids[t], :]
 // ---------------------------------------------------------------------------------------
 __global__ void embed_kernel(const int* ids, const bf16* table, bf16* out, int hidden,
@@ -159,6 +177,20 @@ __global__ void rope_kv_kernel(bf16* qkv, int ld, const int* positions, const in
 // ---------------------------------------------------------------------------------------
 // Host wrappers
 // ---------------------------------------------------------------------------------------
+void forward_tokens(at::Tensor& ids, const at::Tensor& src, const at::Tensor& last,
+                    at::Tensor& err) {
+  const int n = ids.size(0);
+  if (n == 0) return;
+  TORCH_CHECK(ids.scalar_type() == at::kInt && src.scalar_type() == at::kInt &&
+                  last.scalar_type() == at::kInt && src.size(0) >= n && ids.is_contiguous() &&
+                  src.is_contiguous() && last.is_contiguous(),
+              "forward_tokens: contiguous int32 tensors");
+  forward_tokens_kernel<<<(n + 127) / 128, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+      ids.data_ptr<int>(), src.data_ptr<int>(), last.data_ptr<int>(), n,
+      static_cast<int>(last.size(0)), err.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void embedding(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, at::Tensor& err) {
   const int T = ids.size(0);
   if (T == 0) return;

@@ -227,6 +227,8 @@ class EngineConfig:
     device: str = "cuda"
     seed: int = 0
     use_cuda_graphs: bool = True
+    # launch decode step N+1 before reading back step N's ids (host work overlaps the GPU)
+    overlap_decode: bool = True
     model_path: Optional[str] = None
 
 

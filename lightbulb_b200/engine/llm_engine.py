@@ -75,6 +75,14 @@ def derive_num_blocks(cfg: ModelConfig, cache: CacheConfig, tp_size: int, device
     return max(16, avail // per_block)
 
 
+@dataclass
+class _PendingStep:
+    chunks: list                 # decode chunks of the launched step, in row order
+    handle: object               # PendingTokens of the runner
+    marks: list                  # per chunk: (output index, token-list index) of its placeholder
+    rows: Dict[int, int]         # seq_id -> row (the forwarding source for the next step)
+
+
 class LLMEngine:
     def __init__(self, cfg: EngineConfig, packed_weights: dict,
                  tokenizer: Optional[BaseTokenizer] = None, comm=None, tp_rank: int = 0,
@@ -109,6 +117,9 @@ class LLMEngine:
         self.spec = None  # speculative decoder (engine/speculative.py) when configured
         self.kv_policy = None  # KV compression policy (kv/compression.py) when configured
         self.tool_detector = None  # tool-call detection (extras/tools.py) when enabled
+        # overlapped decode: step N+1 is launched before step N's ids are read back
+        self.overlap = bool(getattr(cfg, "overlap_decode", True))
+        self._pending: Optional[_PendingStep] = None
         log.info("engine ready: %d KV blocks of %d tokens (%.1f GiB)", nb, cfg.cache.block_size,
                  self.kv.storage.numel() * 2 / 2**30)
         if cfg.cache.h2o_budget > 0:
@@ -178,7 +189,7 @@ class LLMEngine:
         self.scheduler.abort(request_id)
 
     def has_unfinished(self) -> bool:
-        return self.scheduler.has_work()
+        return self._pending is not None or self.scheduler.has_work()
 
     @staticmethod
     def _setup_comm(comm, cfg: EngineConfig, dev) -> None:
@@ -196,7 +207,7 @@ class LLMEngine:
 
     def has_runnable(self) -> bool:
         """Work that can make progress (requests paused on a tool call wait for a result)."""
-        return bool(self.scheduler.waiting) or any(
+        return self._pending is not None or bool(self.scheduler.waiting) or any(
             s.status != SeqStatus.AWAITING_TOOL for s in self.scheduler.running)
 
     # ---- tool calls (reference src/engine/tool_call.rs, parallel_model_manager.rs) ----------
@@ -230,7 +241,17 @@ class LLMEngine:
 
     # ---------------------------------------------------------------------------------
     def step(self) -> List[RequestOutput]:
+        """One scheduler iteration.  In steady decode (every running sequence decoding, nothing
+        waiting, no speculative / KV-compression / tool-call hooks) the step is overlapped: the
+        next decode step is launched first, with the input ids that are still on the device
+        forwarded there, and the previous step's ids are read back and processed while it runs.
+        The outputs returned are then those of the previous step."""
         with trace.nvtx_range("engine.step"):
+            ok = self._overlap_ok()
+            if self._pending is not None and not ok:
+                return self._collect_pending()          # drain; the next call schedules
+            if ok:
+                return self._step_overlapped()
             if self.spec is not None and self.spec.active:
                 return self.spec.step(self)
             with trace.nvtx_range("schedule"):
@@ -245,6 +266,77 @@ class LLMEngine:
             with trace.nvtx_range("execute"):
                 res = self.runner.execute(so)
             return self._process(res.chunks, res.tokens)
+
+    # ---- overlapped decode ------------------------------------------------------------
+    def _overlap_ok(self) -> bool:
+        if not self.overlap or self.spec is not None or self.kv_policy is not None or \
+                self.tool_detector is not None:
+            return False
+        sch = self.scheduler
+        if sch.waiting or not sch.running:
+            return False
+        bm = self.blocks
+        need = 0
+        running = SeqStatus.RUNNING
+        for s in sch.running:
+            if s.status is not running or s.num_uncomputed != 1:
+                return False
+            need += bm.blocks_needed(s.seq_id, 1)
+        # enough blocks for every sequence: the schedule cannot preempt
+        return need <= bm.num_free_blocks()
+
+    def _step_overlapped(self) -> List[RequestOutput]:
+        prev = self._pending
+        if prev is not None:
+            # a sequence whose pending id is its last (length limit) sits the next step out
+            max_len = self.cfg.scheduler.max_model_len
+            for s in self.scheduler.running:
+                if s.seq_id in prev.rows and (len(s.output_token_ids) >= s.max_new_tokens or
+                                              s.num_tokens >= max_len):
+                    s.hold = True
+        with trace.nvtx_range("schedule"):
+            so = self.scheduler.schedule()
+        if so.prefill or so.preempted:
+            raise RuntimeError("overlapped decode scheduled a prefill or a preemption")
+        if so.empty:
+            return self._collect_pending() if prev is not None else []
+        rows = prev.rows if prev is not None else {}
+        src = [rows.get(c.seq.seq_id, -1) for c in so.decode]
+        with trace.nvtx_range("execute"):
+            res = self.runner.execute(so, src_rows=src, defer=True)
+        marks = []
+        for c in so.decode:
+            c.seq.num_computed_tokens += 1
+            marks.append(c.seq.append_placeholder())
+        self._pending = _PendingStep(so.decode, res.pending, marks,
+                                     {c.seq.seq_id: i for i, c in enumerate(so.decode)})
+        if prev is None:
+            return []
+        return self._collect(prev)
+
+    def _collect_pending(self) -> List[RequestOutput]:
+        p, self._pending = self._pending, None
+        return self._collect(p) if p is not None else []
+
+    def _collect(self, p: "_PendingStep") -> List[RequestOutput]:
+        with trace.nvtx_range("collect"):
+            toks = p.handle.tokens()
+        now = time.perf_counter()
+        self.stats.steps += 1
+        bm = self.blocks
+        outs: List[RequestOutput] = []
+        for c, (oi, ti), tok in zip(p.chunks, p.marks, toks):
+            seq = c.seq
+            seq.hold = False
+            if seq.finished:
+                if len(seq.output_token_ids) > oi:
+                    seq.truncate_output(oi)
+                continue
+            seq.set_output(oi, ti, tok)
+            if bm.has_seq(seq.seq_id):
+                bm.set_tokens(seq.seq_id, [tok])
+            outs.append(self._append_token(seq, tok, now, n_out=oi + 1, n_tok=ti + 1))
+        return outs
 
     def enable_kv_compression(self, kind: str = "h2o", budget: int = 2048, sinks: int = 4,
                               **kw):
@@ -277,8 +369,13 @@ class LLMEngine:
             self.kv_policy.after_step(self)
         return outs
 
-    def _append_token(self, seq: Sequence, tok: int, now: float) -> RequestOutput:
-        seq.append_output(tok)
+    def _append_token(self, seq: Sequence, tok: int, now: float, n_out: Optional[int] = None,
+                      n_tok: Optional[int] = None) -> RequestOutput:
+        """Record sampled id ``tok``.  ``n_out`` / ``n_tok``: the output and token counts up to
+        and including it, when it fills a placeholder (later placeholders may follow)."""
+        if n_out is None:
+            seq.append_output(tok)
+            n_out, n_tok = len(seq.output_token_ids), seq.num_tokens
         if seq.first_token_time is None:
             seq.first_token_time = now
             self.stats.ttfts.append(now - seq.arrival_time)
@@ -301,9 +398,9 @@ class LLMEngine:
                 k = seq.output_text.find(s)
                 if k >= 0:
                     seq.output_text = seq.output_text[:k]
-        elif len(seq.output_token_ids) >= seq.max_new_tokens:
+        elif n_out >= seq.max_new_tokens:
             reason = "length"
-        elif seq.num_tokens >= self.cfg.scheduler.max_model_len:
+        elif n_tok >= self.cfg.scheduler.max_model_len:
             reason = "length"
         call = None
         if reason is None and self.tool_detector is not None and seq.output_text:
@@ -313,11 +410,11 @@ class LLMEngine:
                 seq.pending_tool_call = call
                 seq.status = SeqStatus.AWAITING_TOOL
         if reason is not None:
+            seq.truncate_output(n_out)     # drop a placeholder launched after this token
             self.scheduler.finish(seq, reason)
             self.stats.finished += 1
         return RequestOutput(seq.request_id, [tok], delta, reason is not None, reason,
-                             seq.prompt_len, len(seq.output_token_ids), seq.num_cached_prefix,
-                             call)
+                             seq.prompt_len, n_out, seq.num_cached_prefix, call)
 
     # ---------------------------------------------------------------------------------
     def generate(self, prompts: Union[str, List[str], None] = None,

@@ -33,8 +33,21 @@ DEFAULT_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 160, 192, 224, 256, 
 @dataclass
 class StepResult:
     chunks: List[ScheduledChunk]
-    tokens: List[int]            # one per chunk with needs_logits, in chunk order
+    tokens: Optional[List[int]]  # one per chunk with needs_logits, in chunk order
     logprobs: Optional[List[float]] = None
+    pending: Optional["PendingTokens"] = None   # deferred launch: tokens arrive later
+
+
+class PendingTokens:
+    """Sampled ids of a launched step, copied to pinned host memory behind a CUDA event."""
+
+    def __init__(self, host: torch.Tensor, n: int, event=None):
+        self.host, self.n, self.event = host, n, event
+
+    def tokens(self) -> List[int]:
+        if self.event is not None:
+            self.event.synchronize()
+        return self.host[:self.n].tolist()
 
 
 class _GraphBucket:
@@ -45,8 +58,8 @@ class _GraphBucket:
         dev = r.device
         W = r.max_blocks_per_seq
         self.W = W
-        # int32 layout: ids | pos | slots | seq_lens | cu_q(B+1) | top_k | block_tables(B*W)
-        self.n_int = 6 * bsz + 1 + bsz * W
+        # int32 layout: ids | pos | slots | seq_lens | cu_q(B+1) | top_k | src | block_tables(B*W)
+        self.n_int = 7 * bsz + 1 + bsz * W
         self.ints = torch.zeros(self.n_int, dtype=torch.int32, device=dev)
         self.floats = torch.zeros(2 * bsz, dtype=torch.float32, device=dev)
         self.seeds = torch.zeros(bsz, dtype=torch.int64, device=dev)
@@ -61,9 +74,10 @@ class _GraphBucket:
         self.ids, self.pos, self.slots, self.seq_lens = take(bsz), take(bsz), take(bsz), take(bsz)
         self.cu_q = take(bsz + 1)
         self.top_k = take(bsz)
+        self.src = take(bsz)           # row of the previous step whose sample feeds this row
         self.block_tables = take(bsz * W).view(bsz, W)
         self.temp, self.top_p = self.floats[:bsz], self.floats[bsz:]
-        self.out_tokens = torch.zeros(bsz, dtype=torch.int32, device=dev)
+        self.out_tokens = r.d_last_out[:bsz]   # shared by every bucket: read by the next step
         self.logits_idx = torch.arange(bsz, dtype=torch.int64, device=dev)
         self.splits = ops.decode_splits(bsz, r.model.hkv, r.max_model_len) if r.is_cuda else 1
         self.graph: Optional[torch.cuda.CUDAGraph] = None
@@ -75,6 +89,7 @@ class _GraphBucket:
                             decode_splits=self.splits)
 
     def run(self, runner: "ModelRunner"):
+        ops.forward_tokens(self.ids, self.src, runner.d_last_out)
         logits = runner.model.forward(self.batch(), runner.kv)
         if self.greedy:
             runner.comm.argmax_vocab_parallel(logits, self.out_tokens)
@@ -115,7 +130,12 @@ class ModelRunner:
         ns = self.max_tokens + 1
         self.h_floats = torch.zeros(2 * ns, dtype=torch.float32, pin_memory=pin)
         self.h_seeds = torch.zeros(ns, dtype=torch.int64, pin_memory=pin)
-        self.h_out = torch.zeros(ns, dtype=torch.int32, pin_memory=pin)
+        # two pinned result buffers: a deferred step's ids stay readable while the next
+        # step's copy lands in the other one
+        self.h_outs = [torch.zeros(ns, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
+        self._hout_k = 0
+        # the last step's sampled ids on the device (overlapped decode forwards them)
+        self.d_last_out = torch.zeros(ns, dtype=torch.int32, device=self.device)
         self.d_ints = torch.zeros(n_int, dtype=torch.int32, device=self.device)
         self.d_floats = torch.zeros(2 * ns, dtype=torch.float32, device=self.device)
         self.d_seeds = torch.zeros(ns, dtype=torch.int64, device=self.device)
@@ -187,16 +207,41 @@ class ModelRunner:
         return temps, topk, topp, seeds
 
     # -------------------------------------------------------------------------------
-    def execute(self, so: SchedulerOutput) -> StepResult:
+    def _next_hout(self) -> torch.Tensor:
+        self._hout_k ^= 1
+        return self.h_outs[self._hout_k]
+
+    def _finish_out(self, dev_out: torch.Tensor, n: int, defer: bool):
+        """Copy ``n`` sampled ids to pinned memory; return them, or a pending handle."""
+        if not self.is_cuda:
+            host = dev_out[:n].clone()
+            return PendingTokens(host, n) if defer else host.tolist()
+        h = self._next_hout()
+        h[:n].copy_(dev_out[:n], non_blocking=True)
+        self.d2h_bytes = n * 4
+        if defer:
+            ev = torch.cuda.Event()
+            ev.record()
+            return PendingTokens(h, n, ev)
+        torch.cuda.current_stream().synchronize()
+        return h[:n].tolist()
+
+    def execute(self, so: SchedulerOutput, src_rows: Optional[List[int]] = None,
+                defer: bool = False) -> StepResult:
+        """Run one scheduled step.  ``src_rows[i] >= 0``: decode chunk i's input token is row
+        ``src_rows[i]`` of the previous step's samples (still on the device).  ``defer``:
+        return right after the launch, with the ids behind :class:`PendingTokens`."""
         if so.cow_pairs:
             self.kv.copy_blocks(so.cow_pairs)
         chunks = so.decode + so.prefill
         if not chunks:
             return StepResult([], [])
         if not so.prefill and self.use_graphs and len(chunks) <= self.buckets[-1]:
-            toks = self._run_graph(chunks)
+            toks = self._run_graph(chunks, src_rows, defer)
         else:
-            toks = self._run_eager(chunks, len(so.decode))
+            toks = self._run_eager(chunks, len(so.decode), src_rows, defer)
+        if defer:
+            return StepResult(chunks, None, pending=toks)
         return StepResult(chunks, toks)
 
     # -------------------------------------------------------------------------------
@@ -209,7 +254,7 @@ class ModelRunner:
         return (self.comm is not None and self.comm.world > 1 and
                 all(c.seq.params.temperature <= 0 for c in chunks))
 
-    def _run_graph(self, chunks: List[ScheduledChunk]) -> List[int]:
+    def _run_graph(self, chunks: List[ScheduledChunk], src_rows=None, defer: bool = False):
         B = len(chunks)
         bsz = self.buckets[bisect.bisect_left(self.buckets, B)]
         greedy = self._greedy_variant(chunks)
@@ -222,14 +267,20 @@ class ModelRunner:
         ids, pos, slots = hi[:bsz], hi[bsz:2 * bsz], hi[2 * bsz:3 * bsz]
         seq_lens, cu_q = hi[3 * bsz:4 * bsz], hi[4 * bsz:5 * bsz + 1]
         top_k = hi[5 * bsz + 1:6 * bsz + 1]
-        bt = hi[6 * bsz + 1:].reshape(bsz, W)
+        src = hi[6 * bsz + 1:7 * bsz + 1]
+        bt = hi[7 * bsz + 1:].reshape(bsz, W)
         slots[:] = -1
+        src[:] = -1
         for i, c in enumerate(chunks):
             s = c.seq
             ids[i] = s.last_token
             pos[i] = c.start + getattr(s, "evicted", 0)
             slots[i] = c.slots[0]
             seq_lens[i] = c.start + 1
+        if src_rows is not None:
+            sr = np.asarray(src_rows, dtype=np.int32)
+            src[:B] = sr
+            ids[:B][sr >= 0] = 0
         cu_q[:B + 1] = np.arange(B + 1, dtype=np.int32)
         cu_q[B + 1:] = B
         self._fill_block_tables([c.seq for c in chunks], bt[:B], W)
@@ -249,11 +300,7 @@ class ModelRunner:
         g.graph.replay()
         self._ev_end(ev)
         ops.launch_counter_add(g.launches)
-        out = self.h_out[:bsz]
-        out.copy_(g.out_tokens, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-        self.d2h_bytes = bsz * 4
-        return out[:B].tolist()
+        return self._finish_out(g.out_tokens, B, defer)
 
     def _capture(self, bsz: int, greedy: bool = False) -> _GraphBucket:
         g = _GraphBucket(self, bsz, greedy)
@@ -261,6 +308,7 @@ class ModelRunner:
         g.cu_q.copy_(torch.arange(bsz + 1, dtype=torch.int32))
         g.seq_lens.fill_(1)
         g.slots.fill_(-1)
+        g.src.fill_(-1)
         g.temp.fill_(0.0)
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
@@ -290,7 +338,8 @@ class ModelRunner:
                     if (b, greedy) not in self.graphs:
                         self._capture(b, greedy)
 
-    def _run_eager(self, chunks: List[ScheduledChunk], num_decode: int) -> List[int]:
+    def _run_eager(self, chunks: List[ScheduledChunk], num_decode: int, src_rows=None,
+                   defer: bool = False):
         B = len(chunks)
         T = sum(c.num_tokens for c in chunks)
         width = max((len(self.bm.block_table(c.seq.seq_id)) for c in chunks), default=1)
@@ -309,6 +358,7 @@ class ModelRunner:
         nlog = sum((c.num_tokens if c.logits_all else 1) for c in chunks if c.needs_logits)
         logits_idx = take(nlog)
         top_k = take(nlog)
+        src = take(num_decode)
         bt = take(B * width).reshape(B, width)
         n_int = o
         t = 0
@@ -331,6 +381,12 @@ class ModelRunner:
                 else:
                     logits_idx[li] = t - 1
                     li += 1
+        fwd = src_rows is not None and any(r >= 0 for r in src_rows)
+        if fwd:
+            # decode chunks come first, one token each: token row i is decode chunk i
+            sr = np.asarray(src_rows, dtype=np.int32)
+            src[:] = sr
+            ids[:num_decode][sr >= 0] = 0
         self._fill_block_tables([c.seq for c in chunks], bt, width)
         temps, tk, tp, seeds = self._sampling_rows(chunks)
         top_k[:] = tk
@@ -357,7 +413,10 @@ class ModelRunner:
         d_seq_lens, d_cu_q = dtake(B), dtake(B + 1)
         d_logits_idx = dtake(nlog).long()
         d_top_k = dtake(nlog)
+        d_src = dtake(num_decode)
         d_bt = dtake(B * width).view(B, width)
+        if fwd:
+            ops.forward_tokens(d_ids[:num_decode], d_src, self.d_last_out)
         cu_list = cu_q.tolist()
         ts, tr = prefill_tiles(cu_list, num_decode, self.model.group)
         tiles = torch.tensor([ts, tr], dtype=torch.int32).to(self.device, non_blocking=True) \
@@ -377,11 +436,7 @@ class ModelRunner:
         self.postprocess_logits(logits, df[:nlog], d_top_k, df[nlog:2 * nlog], ds, out,
                                 greedy=self._greedy_variant([c for c in chunks
                                                               if c.needs_logits]))
+        if nlog <= self.d_last_out.shape[0]:
+            self.d_last_out[:nlog].copy_(out)
         self._ev_end(ev)
-        if self.is_cuda:
-            h = self.h_out[:nlog]
-            h.copy_(out, non_blocking=True)
-            torch.cuda.current_stream().synchronize()
-            self.d2h_bytes = nlog * 4
-            return h.tolist()
-        return out.tolist()
+        return self._finish_out(out, nlog, defer)

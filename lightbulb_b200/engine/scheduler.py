@@ -136,7 +136,7 @@ class Scheduler:
         i = 0
         while i < len(self.running):
             seq = self.running[i]
-            if seq.status == SeqStatus.AWAITING_TOOL or seq.num_uncomputed != 1:
+            if seq.status == SeqStatus.AWAITING_TOOL or seq.num_uncomputed != 1 or seq.hold:
                 i += 1
                 continue
             if budget <= 0:
@@ -146,7 +146,9 @@ class Scheduler:
                     break
             if seq not in self.running:
                 continue
-            slots, cow = bm.append_slots(seq.seq_id, 1, [seq.last_token])
+            # a pending id (overlapped decode, < 0) is recorded once it is known (set_tokens)
+            last = seq.last_token
+            slots, cow = bm.append_slots(seq.seq_id, 1, [last] if last >= 0 else [])
             out.cow_pairs += cow
             out.decode.append(ScheduledChunk(seq, seq.num_computed_tokens, 1, slots, True))
             budget -= 1

@@ -16,6 +16,7 @@ from typing import List, Optional
 from .sampling import SamplingParams
 
 _seq_ids = itertools.count()
+PENDING_TOKEN = -1   # output slot whose id is still on the device (overlapped decode)
 
 
 class SeqStatus(enum.Enum):
@@ -52,6 +53,9 @@ class Sequence:
     pending_tool_call: Optional[dict] = None
     injected_tokens: int = 0
     tool_scan_from: int = 0          # output_text offset already scanned for tool calls
+    # overlapped decode: the newest output is a placeholder (PENDING_TOKEN) until its step's
+    # ids are read back; `hold` keeps a sequence that is about to finish out of the next step
+    hold: bool = False
 
     def __post_init__(self) -> None:
         # prompt + generated ids in one list, appended in place (never rebuilt per step)
@@ -60,6 +64,16 @@ class Sequence:
     def append_output(self, tok: int) -> None:
         self.output_token_ids.append(tok)
         self._tokens.append(tok)
+
+    def append_placeholder(self):
+        """Append a PENDING_TOKEN output; returns its (output index, token-list index)."""
+        self.append_output(PENDING_TOKEN)
+        return len(self.output_token_ids) - 1, len(self._tokens) - 1
+
+    def set_output(self, out_idx: int, tok_idx: int, tok: int) -> None:
+        """Fill a placeholder appended by :meth:`append_placeholder`."""
+        self.output_token_ids[out_idx] = tok
+        self._tokens[tok_idx] = tok
 
     def truncate_output(self, n: int) -> None:
         """Keep the first ``n`` generated tokens (speculative rollback of the newest outputs,

@@ -207,6 +207,20 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, residual: Optional[tor
     return out
 
 
+def forward_tokens(ids: torch.Tensor, src: torch.Tensor, last: torch.Tensor) -> None:
+    """In place: ``ids[i] = last[src[i]]`` where ``src[i] >= 0`` (overlapped decode feeds the
+    previous step's sampled tokens without a host round trip)."""
+    if ids.is_cuda:
+        _need_c().forward_tokens(ids, src, last, scratch(ids.device).err)
+        _launches[0] += 1
+        return
+    n = ids.shape[0]
+    s = src[:n].long()
+    m = s >= 0
+    if bool(m.any()):
+        ids[m] = last[s[m]].to(ids.dtype)
+
+
 def embedding(ids: torch.Tensor, table: torch.Tensor, out: Optional[torch.Tensor] = None):
     if out is None:
         out = torch.empty(ids.shape[0], table.shape[1], dtype=table.dtype, device=table.device)
