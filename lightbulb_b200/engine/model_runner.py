@@ -125,11 +125,17 @@ class ModelRunner:
         self.comm = comm
         pin = self.is_cuda
         n_int = 6 * self.max_tokens + 3 * (max_num_seqs + 1) + max_num_seqs * self.max_blocks_per_seq
-        self.h_ints = torch.zeros(n_int, dtype=torch.int32, pin_memory=pin)
         # sampled rows per step: one per sequence, or every row of a verify chunk
         ns = self.max_tokens + 1
-        self.h_floats = torch.zeros(2 * ns, dtype=torch.float32, pin_memory=pin)
-        self.h_seeds = torch.zeros(ns, dtype=torch.int64, pin_memory=pin)
+        # Two sets of pinned input buffers, alternated per launch: with overlapped decode the
+        # host fills step N+1's inputs while step N's H2D copy may still be queued behind
+        # step N-1, so a step's buffer is rewritten only two launches later (after its ids
+        # were read back, which orders its copies before).
+        self._h_in = [(torch.zeros(n_int, dtype=torch.int32, pin_memory=pin),
+                       torch.zeros(2 * ns, dtype=torch.float32, pin_memory=pin),
+                       torch.zeros(ns, dtype=torch.int64, pin_memory=pin)) for _ in range(2)]
+        self._h_in_k = 0
+        self.h_ints, self.h_floats, self.h_seeds = self._h_in[0]
         # two pinned result buffers: a deferred step's ids stay readable while the next
         # step's copy lands in the other one
         self.h_outs = [torch.zeros(ns, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
@@ -207,6 +213,10 @@ class ModelRunner:
         return temps, topk, topp, seeds
 
     # -------------------------------------------------------------------------------
+    def _next_host_inputs(self) -> None:
+        self._h_in_k ^= 1
+        self.h_ints, self.h_floats, self.h_seeds = self._h_in[self._h_in_k]
+
     def _next_hout(self) -> torch.Tensor:
         self._hout_k ^= 1
         return self.h_outs[self._hout_k]
@@ -262,6 +272,7 @@ class ModelRunner:
         if g is None:
             g = self._capture(bsz, greedy)
         W = g.W
+        self._next_host_inputs()
         hi = self.h_ints[:g.n_int].numpy()
         hi[:] = 0
         ids, pos, slots = hi[:bsz], hi[bsz:2 * bsz], hi[2 * bsz:3 * bsz]
@@ -344,6 +355,7 @@ class ModelRunner:
         T = sum(c.num_tokens for c in chunks)
         width = max((len(self.bm.block_table(c.seq.seq_id)) for c in chunks), default=1)
         width = max(width, 1)
+        self._next_host_inputs()
         hi = self.h_ints.numpy()
         o = 0
 

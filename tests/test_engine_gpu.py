@@ -84,3 +84,34 @@ def test_engine_padded_heads_gpu(hidden, heads, kv):
         for i, t in enumerate(s.output_token_ids):
             top2 = torch.topk(lg[i], 2).values
             assert int(torch.argmax(lg[i])) == t or (top2[0] - top2[1]) < 0.05
+
+
+def test_overlapped_decode_matches_sync_gpu():
+    # CUDA-graph decode with overlap (next step launched before the previous ids are read
+    # back; pinned inputs double-buffered) must emit the synchronous engine's tokens
+    import random
+    cfg = get_preset("tiny-test", vocab_size=1024)
+    w = random_weights(cfg, seed=7, std=0.05)
+    packed = pack_model(cfg, w, dtype=torch.bfloat16, device="cuda")
+    rng = random.Random(2)
+    prompts = [[rng.randrange(3, 1000) for _ in range(rng.randint(3, 70))] for _ in range(12)]
+    params = [SamplingParams(temperature=0.0 if i % 2 else 0.8, seed=i, top_k=50,
+                             max_tokens=5 + 3 * i, ignore_eos=True) for i in range(12)]
+    outs = []
+    for overlap in (False, True):
+        ecfg = EngineConfig(model=cfg, cache=CacheConfig(num_blocks=256, block_size=16),
+                            scheduler=SchedulerConfig(max_num_seqs=16, max_num_batched_tokens=256,
+                                                      chunk_size=128, max_model_len=512),
+                            use_cuda_graphs=True, overlap_decode=overlap)
+        eng = LLMEngine(ecfg, packed)
+        seqs = [eng.add_request(f"r{i}", prompt_token_ids=p, params=sp)
+                for i, (p, sp) in enumerate(zip(prompts, params))]
+        n_pending = 0
+        while eng.has_unfinished():
+            eng.step()
+            n_pending += eng._pending is not None
+        ops.check_errors()
+        assert (n_pending > 0) == overlap
+        outs.append([s.output_token_ids for s in seqs])
+    assert outs[0] == outs[1]
+    assert [len(o) for o in outs[1]] == [sp.max_tokens for sp in params]
