@@ -314,6 +314,9 @@ class ModelRunner:
         return self._finish_out(g.out_tokens, B, defer)
 
     def _capture(self, bsz: int, greedy: bool = False) -> _GraphBucket:
+        # the warm-up runs write dummy samples into the shared last-ids buffer, which an
+        # overlapped step launched next still has to read: keep its contents
+        saved = self.d_last_out.clone()
         g = _GraphBucket(self, bsz, greedy)
         # valid dummy inputs: every row points at block 0 with one token, no KV write
         g.cu_q.copy_(torch.arange(bsz + 1, dtype=torch.int32))
@@ -337,6 +340,7 @@ class ModelRunner:
         g.launches = ops.launch_counter_value() - n0
         ops.launch_counter_add(-g.launches)  # capture launched nothing
         torch.cuda.synchronize()
+        self.d_last_out.copy_(saved)
         g.graph = graph
         self.graphs[(bsz, greedy)] = g
         return g
