@@ -25,6 +25,9 @@ void gemm_bf16_tp(const at::Tensor& A, const at::Tensor& W, at::Tensor& C, int64
                   int64_t done_counter_ptr, int64_t trace_ptr,
                   const c10::optional<at::Tensor>& ws);
 int64_t allreduce_buffer_bytes(int64_t max_elems, int64_t world);
+void gemm_bf16_pair(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
+                    const c10::optional<at::Tensor>& residual, int64_t mode, at::Tensor& err,
+                    int64_t bt);
 void allreduce_prepare(int64_t base, int64_t max_elems, int64_t world);
 void allreduce_p2p(at::Tensor& out, const at::Tensor& inp, std::vector<int64_t> bases,
                    int64_t rank, int64_t n_elems, int64_t max_elems, int64_t ctas,
@@ -77,6 +80,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("trace_ptr") = 0, py::arg("ws") = py::none());
   m.def("allreduce_buffer_bytes", &lb::allreduce_buffer_bytes);
   m.def("allreduce_prepare", &lb::allreduce_prepare);
+  m.def("gemm_bf16_pair", &lb::gemm_bf16_pair, "bf16 GEMM on SM pairs (tcgen05 cta_group::2)",
+        py::arg("A"), py::arg("W"), py::arg("C"), py::arg("residual"), py::arg("mode"),
+        py::arg("err"), py::arg("bt") = 0);
   m.def("allreduce_p2p", &lb::allreduce_p2p, "two-shot all-reduce over NVLink peer memory");
   m.def("ipc_alloc", &lb::ipc_alloc);
   m.def("ipc_free", &lb::ipc_free);

@@ -426,6 +426,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+}  // namespace lb
+
+#include "gemm_tc2.cuh"
+
+namespace lb {
+
 // ======================================================================================
 // Cluster split-K variant for small token counts (decode).  The S CTAs of a thread-block
 // cluster own the same 128 x BT output tile and split K; the fp32 accumulators are combined
@@ -912,6 +918,112 @@ static void launch_cluster(const CUtensorMap& tw, const CUtensorMap& tx, const C
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_tc_cluster_kernel<BT, STAGES>, tw, tx, tc, a));
+}
+
+// SM-pair persistent GEMM (gemm_tc2.cuh): 256-row weight tiles, clusters of 2 CTAs.
+template <int BT, int STAGES>
+static void launch_pair(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a,
+                        cudaStream_t st) {
+  using L = tc2::Smem<BT, STAGES>;
+  static bool attr = false;
+  if (!attr) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_tc2_kernel<BT, STAGES>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
+    attr = true;
+  }
+  const int n_tiles = (a.N + 2 * BW - 1) / (2 * BW);
+  const int units = a.m_tiles * n_tiles;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr2[1];
+  attr2[0].id = cudaLaunchAttributeClusterDimension;
+  attr2[0].val.clusterDim.x = 2;
+  attr2[0].val.clusterDim.y = 1;
+  attr2[0].val.clusterDim.z = 1;
+  cfg.attrs = attr2;
+  cfg.numAttrs = 1;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = L::TOTAL;
+  // persistent grid: as many pairs as can be resident at once (SM pairs within a GPC)
+  static int resident = 0;
+  if (resident == 0) {
+    cfg.gridDim = dim3(num_sms());
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_tc2_kernel<BT, STAGES>, &cfg) != cudaSuccess ||
+        n <= 0) {
+      cudaGetLastError();
+      n = num_sms() / 2;
+    }
+    resident = n;
+  }
+  const int pairs = std::max(1, std::min(units, resident));
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.stream = st;
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<BT, STAGES>, tw, tx, a));
+}
+
+// Token tile of the pair kernel for M tokens (0 = not worth it: the single-SM kernels win).
+static int pair_bt(int M) { return M > 128 ? 256 : M > 64 ? 128 : 0; }
+
+// C = A . W^T on SM pairs (no split-K).  bt: 128 or 256 (0 = by M).
+static void gemm_pair_launch(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
+                             const bf16* residual, int ldr, int64_t mode, at::Tensor& err, int BT,
+                             cudaStream_t st) {
+  const int M = A.size(0), K = A.size(1), N = W.size(0);
+  GemmArgs a = {};
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.m_tiles = (M + BT - 1) / BT;
+  a.n_tiles = (N + BW - 1) / BW;
+  a.splits = 1;
+  a.kb_total = (K + BK - 1) / BK;
+  a.kb_per_split = a.kb_total;
+  a.C = C.data_ptr();
+  a.ldc = C.stride(0);
+  a.residual = residual;
+  a.ldr = ldr;
+  a.mode = static_cast<int>(mode);
+  a.err = err.data_ptr<int>();
+  a.vec_ok = (reinterpret_cast<uintptr_t>(C.data_ptr()) % 16 == 0) && (C.stride(0) % 4 == 0);
+  const CUtensorMap tw = make_tmap_bf16_2d(W.data_ptr(), K, N, W.stride(0) * 2, BK, BW,
+                                           CU_TENSOR_MAP_SWIZZLE_128B);
+  const CUtensorMap tx = make_tmap_bf16_2d(A.data_ptr(), K, M, A.stride(0) * 2, BK, BT / 2,
+                                           CU_TENSOR_MAP_SWIZZLE_128B);
+  if (BT == 256) launch_pair<256, 6>(tw, tx, a, st);
+  else launch_pair<128, 8>(tw, tx, a, st);
+}
+
+// Test / benchmark entry: the SM-pair kernel regardless of the dispatch policy.
+void gemm_bf16_pair(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
+                    const c10::optional<at::Tensor>& residual, int64_t mode, at::Tensor& err,
+                    int64_t bt) {
+  TORCH_CHECK(A.is_cuda() && W.is_cuda() && C.is_cuda(), "gemm_pair: CUDA tensors");
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && W.scalar_type() == at::kBFloat16, "bf16 A, W");
+  TORCH_CHECK(A.dim() == 2 && W.dim() == 2 && C.dim() == 2 && A.stride(1) == 1 &&
+                  W.stride(1) == 1 && C.stride(1) == 1, "gemm_pair: 2-D, inner stride 1");
+  const int M = A.size(0), K = A.size(1), N = W.size(0);
+  TORCH_CHECK(W.size(1) == K && K % 8 == 0, "gemm_pair: K");
+  if (M == 0) return;
+  if (mode == kEpiSwiGLU) {
+    TORCH_CHECK(N % 128 == 0 && C.size(1) >= N / 2 && C.scalar_type() == at::kBFloat16, "swiglu");
+  } else if (mode == kEpiF32) {
+    TORCH_CHECK(C.scalar_type() == at::kFloat && C.size(1) >= N, "f32 out");
+  } else {
+    TORCH_CHECK(C.scalar_type() == at::kBFloat16 && C.size(1) >= N, "bf16 out");
+  }
+  TORCH_CHECK(C.size(0) >= M, "gemm_pair: C rows");
+  const bf16* res = nullptr;
+  int ldr = 0;
+  if (residual.has_value() && residual->defined()) {
+    TORCH_CHECK(mode == kEpiStore && residual->scalar_type() == at::kBFloat16 &&
+                    residual->stride(1) == 1, "residual");
+    res = reinterpret_cast<const bf16*>(residual->data_ptr());
+    ldr = residual->stride(0);
+  }
+  int BT = bt > 0 ? static_cast<int>(bt) : pair_bt(M);
+  if (BT == 0) BT = 128;
+  TORCH_CHECK(BT == 128 || BT == 256, "gemm_pair: token tile 128 or 256");
+  gemm_pair_launch(A, W, C, res, ldr, mode, err, BT, at::cuda::getCurrentCUDAStream());
 }
 
 void gemm_bf16(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,

@@ -161,6 +161,21 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
     return out
 
 
+def gemm_pair(a: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
+              residual: Optional[torch.Tensor] = None, mode: int = EPI_STORE,
+              bt: int = 0) -> torch.Tensor:
+    """:func:`gemm` on SM pairs (tcgen05 ``cta_group::2``, 256-row weight tiles), bypassing the
+    dispatch policy (tests and benchmarks)."""
+    m, n = a.shape[0], w.shape[0]
+    if out is None:
+        cols = n // 2 if mode == EPI_SWIGLU else n
+        dt = torch.float32 if mode == EPI_F32 else torch.bfloat16
+        out = torch.empty(m, cols, dtype=dt, device=a.device)
+    _need_c().gemm_bf16_pair(a, w, out, residual, mode, scratch(a.device).err, bt)
+    _launches[0] += 1
+    return out
+
+
 def gemm_quant(a: torch.Tensor, w, out: Optional[torch.Tensor] = None, mode: int = EPI_STORE,
                splits: int = 0) -> torch.Tensor:
     """``a @ dequant(w).T`` for a :class:`~lightbulb_b200.formats.quant.QuantWeight`."""

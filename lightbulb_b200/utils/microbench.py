@@ -94,6 +94,15 @@ def bench_gemm(m, n, k, copies=None, mode=ops.EPI_STORE, bt=0, splits=0, iters=2
         it[0] += 1
 
     us_cublas = time_graph(run_cublas, calls=max(copies, iters))
+    us_pair = None
+    if m > 64:
+        it[0] = 0
+
+        def run_pair():
+            ops.gemm_pair(a, ws[it[0] % copies], mode=mode)
+            it[0] += 1
+
+        us_pair = round(time_graph(run_pair, calls=max(copies, iters)), 2)
     flops = 2 * m * n * k
     byts = wbytes + m * k * 2 + m * n * (4 if mode == ops.EPI_F32 else 2)
     t_roof = max(flops / fl, byts / bw) * 1e6
@@ -101,7 +110,8 @@ def bench_gemm(m, n, k, copies=None, mode=ops.EPI_STORE, bt=0, splits=0, iters=2
     return {"op": "gemm", "m": m, "n": n, "k": k, "us": round(us, 2),
             "tflops": round(flops / us / 1e6, 1), "gbs": round(byts / us / 1e3, 1),
             "roofline_us": round(t_roof, 2), "frac_of_" + src: round(t_roof / us, 3),
-            "plan_bt_splits": plan[:2], "cublas_us": round(us_cublas, 2)}
+            "plan_bt_splits": plan[:2], "cublas_us": round(us_cublas, 2),
+            "pair_us": us_pair}
 
 
 def bench_gemm_quant(m, n, k, kind="awq", iters=20):

@@ -281,3 +281,37 @@ def test_paged_decode_tma_vs_cpasync(hq, hkv, splits):
     ops.check_errors()
     assert _rel(outs["tma"], ref) < 2e-2
     assert _rel(outs["cpasync"], ref) < 2e-2
+
+
+@pytest.mark.parametrize("m,n,k,bt", [(256, 1024, 4096, 0), (100, 640, 1024, 128),
+                                      (300, 384, 2048, 256), (2048, 2048, 1024, 0),
+                                      (129, 4096, 512, 128), (77, 256, 8200, 128)])
+def test_gemm_pair(m, n, k, bt):
+    # SM-pair kernel (tcgen05 cta_group::2): partial weight tiles, partial token tiles, K tails
+    torch.manual_seed(m + n + k)
+    a = torch.randn(m, k, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(n, k, device=DEV) * 0.05).to(torch.bfloat16)
+    ref = a.float() @ w.float().T
+    for _ in range(2):
+        out = ops.gemm_pair(a, w, bt=bt)
+        torch.cuda.synchronize()
+        ops.check_errors()
+        assert _rel(out, ref) < 1e-2
+
+
+def test_gemm_pair_epilogues():
+    from lightbulb_b200.models.weights import interleave_gate_up
+    m, f, k = 200, 640, 1024
+    a = torch.randn(m, k, device=DEV).to(torch.bfloat16)
+    g = (torch.randn(f, k, device=DEV) * 0.05).to(torch.bfloat16)
+    u = (torch.randn(f, k, device=DEV) * 0.05).to(torch.bfloat16)
+    w = interleave_gate_up(g, u)
+    ref = torch.nn.functional.silu(a.float() @ g.float().T) * (a.float() @ u.float().T)
+    out = ops.gemm_pair(a, w, mode=ops.EPI_SWIGLU)
+    assert out.shape == (m, f) and _rel(out, ref) < 1e-2
+    r = torch.randn(m, 2 * f, device=DEV).to(torch.bfloat16)
+    full = a.float() @ w.float().T
+    assert _rel(ops.gemm_pair(a, w, residual=r), full + r.float()) < 1e-2
+    o32 = ops.gemm_pair(a, w, mode=ops.EPI_F32)
+    assert o32.dtype == torch.float32 and _rel(o32, full) < 5e-3
+    ops.check_errors()
