@@ -27,6 +27,7 @@
 
 #include <mutex>
 
+#include <cmath>
 #include <cstring>
 
 #include "cluster_rs.cuh"
@@ -73,7 +74,55 @@ struct GemmArgs {
   int vec_ok;                 // C base 16-byte aligned and ldc % 4 == 0: vector stores
   TpLink tp;
   int tma_out;                // cluster kernel: output tiles through the tensor map tmC
+  int sk_q;                   // > 0: stream-K, k-blocks per CTA over the (tile, k-block) space
 };
+
+// Work of one persistent CTA, as segments (tile, split, k-block range).
+//  * data-parallel / split-K: units blockIdx.x, +gridDim.x, ... of tiles x splits;
+//  * stream-K (sk_q > 0): the contiguous range [b * q, (b + 1) * q) of the linearised
+//    (tile, k-block) space, cut at tile boundaries.  Only a CTA's first segment can start
+//    inside a tile (it then contributes a partial); a segment that starts a tile but ends
+//    inside it belongs to the tile's finisher, which adds the following CTAs' partials.
+struct WorkIter {
+  int u, g, g1;
+  __device__ __forceinline__ void begin(const GemmArgs& a) {
+    if (a.sk_q > 0) {
+      const long long tot = static_cast<long long>(a.m_tiles) * a.n_tiles * a.kb_total;
+      g = static_cast<int>(min(static_cast<long long>(blockIdx.x) * a.sk_q, tot));
+      g1 = static_cast<int>(min(static_cast<long long>(g) + a.sk_q, tot));
+    } else {
+      u = blockIdx.x;
+    }
+  }
+  // tile index t (mt * n_tiles + nt), split index s (data-parallel only), k-block range.
+  __device__ __forceinline__ bool next(const GemmArgs& a, int& t, int& s, int& kb0, int& kb1) {
+    if (a.sk_q > 0) {
+      if (g >= g1) return false;
+      t = g / a.kb_total;
+      kb0 = g - t * a.kb_total;
+      kb1 = min(a.kb_total, kb0 + (g1 - g));
+      s = 0;
+      g += kb1 - kb0;
+      return true;
+    }
+    if (u >= a.m_tiles * a.n_tiles * a.splits) return false;
+    s = u % a.splits;
+    t = u / a.splits;
+    kb0 = s * a.kb_per_split;
+    kb1 = min(kb0 + a.kb_per_split, a.kb_total);
+    u += gridDim.x;
+    return true;
+  }
+};
+
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 
 __device__ __forceinline__ int ld_acquire_sys(const int* p) {
   int v;
@@ -138,6 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* s_last = reinterpret_cast<volatile int*>(tmem_slot + 2);
   volatile int* s_go = reinterpret_cast<volatile int*>(tmem_slot + 4);  // [2]
+  volatile int* s_fin = reinterpret_cast<volatile int*>(tmem_slot + 6);  // [2] stream-K finisher
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -168,15 +218,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int total = a.m_tiles * a.n_tiles * a.splits;
-  // unit -> (m tile, n tile, split); consecutive units share the token tile so that the
+  // tile t -> (m tile, n tile); consecutive tiles share the token tile so that the
   // activation stays in L2 while each weight tile is streamed once.
-  auto decode_unit = [&](int u, int& mt, int& nt, int& s) {
-    s = u % a.splits;
-    int t = u / a.splits;
-    nt = t % a.n_tiles;
-    mt = t / a.n_tiles;
-  };
 
   uint32_t issued_mask = 0, issued_parity = 0;  // producer bookkeeping for abort drain
 
@@ -186,11 +229,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t px = policy_evict_last();
       int stage = 0;
       uint32_t phase = 0;
-      for (int u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x) {
-        int mt, nt, s;
-        decode_unit(u, mt, nt, s);
-        const int kb0 = s * a.kb_per_split;
-        const int kb1 = min(kb0 + a.kb_per_split, a.kb_total);
+      WorkIter w;
+      w.begin(a);
+      int t, s, kb0, kb1;
+      while (!*abort_flag && w.next(a, t, s, kb0, kb1)) {
+        const int nt = t % a.n_tiles, mt = t / a.n_tiles;
         bool ok = true;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
@@ -218,11 +261,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
-      for (int u = blockIdx.x; u < total && !*abort_flag; u += gridDim.x, ++it) {
-        int mt, nt, s;
-        decode_unit(u, mt, nt, s);
-        const int kb0 = s * a.kb_per_split;
-        const int kb1 = min(kb0 + a.kb_per_split, a.kb_total);
+      WorkIter w;
+      w.begin(a);
+      int t, s, kb0, kb1;
+      for (; !*abort_flag && w.next(a, t, s, kb0, kb1); ++it) {
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag)) {
@@ -265,9 +307,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = quad * 32 + lane;    // weight row within the tile == TMEM lane
     const int etid = threadIdx.x - 64;   // 0..127
     int it = 0;
-    for (int u = blockIdx.x; u < total; u += gridDim.x, ++it) {
-      int mt, nt, s;
-      decode_unit(u, mt, nt, s);
+    WorkIter w;
+    w.begin(a);
+    int t, s, kb0, kb1;
+    for (; w.next(a, t, s, kb0, kb1); ++it) {
+      const int nt = t % a.n_tiles, mt = t / a.n_tiles;
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       // One thread waits (bounded); the decision is broadcast so that all 128 epilogue
@@ -286,7 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * BT);
-      const int tile = mt * a.n_tiles + nt;
+      const int tile = t;
       const int m0 = mt * BT;
       const int n = nt * BW + row;
 
@@ -340,7 +384,83 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
 
       float v[CH];
-      if (a.splits == 1) {
+      const bool sk_part = a.sk_q > 0 && kb0 > 0;                       // contributor
+      const bool sk_fin = a.sk_q > 0 && kb0 == 0 && kb1 < a.kb_total;   // finisher
+      if (sk_part) {
+        // partial of k-blocks [kb0, kb1) -> this CTA's slot; the tile's finisher adds it
+        float* wsp = a.ws + static_cast<size_t>(blockIdx.x) * BT * BW;
+#pragma unroll 1
+        for (int c = 0; c < BT; c += CH) {
+          uint32_t r[CH];
+          if constexpr (CH == 32) {
+            tmem_ld32(tbase + c, *reinterpret_cast<uint32_t(*)[32]>(r));
+          } else {
+            tmem_ld16(tbase + c, *reinterpret_cast<uint32_t(*)[16]>(r));
+          }
+          tc_wait_ld();
+          if (c + CH >= BT) {
+            tc_fence_before();
+            mbar_arrive(&tempty[acc]);
+          }
+#pragma unroll
+          for (int j = 0; j < CH; ++j) __stcg(&wsp[(c + j) * BW + row], __uint_as_float(r[j]));
+        }
+        __threadfence();
+        named_bar_sync(1, 128);
+        if (etid == 0) st_release_gpu(&a.counters[blockIdx.x], 1);
+      } else if (sk_fin) {
+        // contributors: the following CTAs whose ranges start inside this tile
+        const long long tile_end = static_cast<long long>(t + 1) * a.kb_total;
+        int c_last = blockIdx.x;
+        while (c_last + 1 < static_cast<int>(gridDim.x) &&
+               static_cast<long long>(c_last + 1) * a.sk_q < tile_end)
+          ++c_last;
+        if (etid == 0) {
+          int go = 1;
+          for (int c2 = blockIdx.x + 1; c2 <= c_last && go; ++c2) {
+            const uint64_t t0 = globaltimer_ns();
+            uint32_t spins = 0;
+            while (ld_acquire_gpu(&a.counters[c2]) == 0) {
+              if ((++spins & 63u) == 0 && globaltimer_ns() - t0 > kWaitBudgetNs) {
+                record_error(a.err, kErrTimeoutPeer);
+                *abort_flag = 1;
+                go = 0;
+                break;
+              }
+            }
+            if (go) a.counters[c2] = 0;   // one consumer per contribution: re-armed for the next launch
+          }
+          s_fin[it & 1] = go;
+        }
+        named_bar_sync(1, 128);
+        const bool have = s_fin[it & 1] != 0;
+#pragma unroll 1
+        for (int c = 0; c < BT; c += CH) {
+          uint32_t r[CH];
+          if constexpr (CH == 32) {
+            tmem_ld32(tbase + c, *reinterpret_cast<uint32_t(*)[32]>(r));
+          } else {
+            tmem_ld16(tbase + c, *reinterpret_cast<uint32_t(*)[16]>(r));
+          }
+          tc_wait_ld();
+          if (c + CH >= BT) {
+            tc_fence_before();
+            mbar_arrive(&tempty[acc]);
+          }
+#pragma unroll
+          for (int j = 0; j < CH; ++j) v[j] = __uint_as_float(r[j]);
+          if (have) {
+            // k order: this CTA's head first, then the contributors in CTA order
+            for (int c2 = blockIdx.x + 1; c2 <= c_last; ++c2) {
+              const float* p = a.ws + static_cast<size_t>(c2) * BT * BW;
+#pragma unroll
+              for (int j = 0; j < CH; ++j) v[j] += __ldcg(&p[(c + j) * BW + row]);
+            }
+            emit(v, c);
+          }
+        }
+        if (!have) break;
+      } else if (a.splits == 1) {
 #pragma unroll 1
         for (int c = 0; c < BT; c += CH) {
           uint32_t r[CH];
@@ -1026,6 +1146,17 @@ void gemm_bf16_pair(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
   gemm_pair_launch(A, W, C, res, ldr, mode, err, BT, at::cuda::getCurrentCUDAStream());
 }
 
+// `splits` value that selects stream-K in the persistent kernel.
+constexpr int64_t kSplitsStreamK = 1000;
+
+// Stream-K quantum: k-blocks per CTA so that ceil(total / q) CTAs (at most one per SM, all
+// resident: finishers wait on contributors) share tiles x kb_total k-blocks evenly.
+static int streamk_q(int tiles, int kb_total) {
+  const long long tot = static_cast<long long>(tiles) * kb_total;
+  const long long g = std::min<long long>(num_sms(), tot);
+  return static_cast<int>((tot + g - 1) / g);
+}
+
 void gemm_bf16(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
                const c10::optional<at::Tensor>& residual, int64_t mode, at::Tensor& ws,
                at::Tensor& counters, at::Tensor& err, int64_t bt, int64_t splits,
@@ -1048,7 +1179,22 @@ void gemm_bf16(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
   } else {
     TORCH_CHECK(C.scalar_type() == at::kBFloat16 && C.size(1) >= N && C.size(0) >= M, "bf16 out");
   }
-  auto plan = gemm_plan(M, N, K, bt, splits);
+  // Stream-K pays one fp32 partial per CTA; it wins only when every CTA covers many tiles and
+  // the data-parallel tail wave would idle (measured: 2048 x 28672 x 4096, 488 -> 438 us; at
+  // 3.5 tiles per CTA and below the per-thread fixup costs more than the wave it saves).
+  bool stream_k = splits == kSplitsStreamK;
+  if (splits == 0) {
+    const int BTp = bt > 0 ? static_cast<int>(bt) : pick_bt(M);
+    const int tl = ((M + BTp - 1) / BTp) * ((N + BW - 1) / BW);
+    const int kbt = (K + BK - 1) / BK;
+    const int sms = num_sms();
+    const double waves = static_cast<double>(tl) / sms;
+    const double eff = waves / std::ceil(waves);
+    stream_k = tl >= 8 * sms && eff < 0.95 &&
+               ws.numel() >= static_cast<int64_t>(sms) * BTp * BW && counters.numel() >= sms &&
+               kbt >= 4;
+  }
+  auto plan = gemm_plan(M, N, K, bt, stream_k ? 1 : splits);
   const int BT = plan[0];
   int sp = plan[1];
   const int tiles = plan[2];
@@ -1110,7 +1256,16 @@ void gemm_bf16(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
     return;
   }
   const int units = a.m_tiles * a.n_tiles * a.splits;
-  const int grid = std::min(units, num_sms());
+  int grid = std::min(units, num_sms());
+  if (stream_k) {
+    const int q = streamk_q(tiles, kb_total);
+    grid = static_cast<int>((static_cast<long long>(tiles) * kb_total + q - 1) / q);
+    TORCH_CHECK(ws.numel() >= static_cast<int64_t>(grid) * BT * BW && counters.numel() >= grid,
+                "gemm: stream-K workspace too small");
+    a.sk_q = q;
+    a.ws = ws.data_ptr<float>();
+    a.counters = counters.data_ptr<int>();
+  }
   switch (BT) {
     case 16: launch_bt<16, 8>(tw, tx, a, grid, st); break;
     case 32: launch_bt<32, 8>(tw, tx, a, grid, st); break;

@@ -22,6 +22,7 @@ else:
     _C_ERR = None
 
 EPI_STORE, EPI_SWIGLU, EPI_F32 = 0, 1, 2
+SPLITS_STREAMK = 1000   # gemm(splits=...): stream-K over (tile, k-block) in the persistent kernel
 
 # Decode attention implementation: "tma" (warp-specialised TMA pipeline, default) or
 # "cpasync" (the generic paged kernel, also used for non-16 block sizes).

@@ -315,3 +315,39 @@ def test_gemm_pair_epilogues():
     o32 = ops.gemm_pair(a, w, mode=ops.EPI_F32)
     assert o32.dtype == torch.float32 and _rel(o32, full) < 5e-3
     ops.check_errors()
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 6144, 4096), (256, 4096, 14336), (256, 28672, 1024),
+                                   (16, 4096, 4096), (77, 1000, 2048), (300, 384, 8200),
+                                   (4096, 1024, 1024)])
+def test_gemm_streamk(m, n, k):
+    # stream-K: CTA ranges cut tiles at arbitrary k-blocks; finishers add partials in k order
+    torch.manual_seed(m + n + k)
+    a = torch.randn(m, k, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(n, k, device=DEV) * 0.05).to(torch.bfloat16)
+    ref = a.float() @ w.float().T
+    outs = []
+    for _ in range(3):   # flags re-armed between launches
+        outs.append(ops.gemm(a, w, splits=ops.SPLITS_STREAMK))
+        torch.cuda.synchronize()
+        ops.check_errors()
+        assert _rel(outs[-1], ref) < 1e-2
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])   # deterministic
+
+
+def test_gemm_streamk_epilogues():
+    from lightbulb_b200.models.weights import interleave_gate_up
+    m, f, k = 256, 1536, 4096
+    a = torch.randn(m, k, device=DEV).to(torch.bfloat16)
+    g = (torch.randn(f, k, device=DEV) * 0.05).to(torch.bfloat16)
+    u = (torch.randn(f, k, device=DEV) * 0.05).to(torch.bfloat16)
+    w = interleave_gate_up(g, u)
+    ref = torch.nn.functional.silu(a.float() @ g.float().T) * (a.float() @ u.float().T)
+    out = ops.gemm(a, w, mode=ops.EPI_SWIGLU, splits=ops.SPLITS_STREAMK)
+    assert out.shape == (m, f) and _rel(out, ref) < 1e-2
+    r = torch.randn(m, 2 * f, device=DEV).to(torch.bfloat16)
+    full = a.float() @ w.float().T
+    assert _rel(ops.gemm(a, w, residual=r, splits=ops.SPLITS_STREAMK), full + r.float()) < 1e-2
+    o32 = ops.gemm(a, w, mode=ops.EPI_F32, splits=ops.SPLITS_STREAMK)
+    assert o32.dtype == torch.float32 and _rel(o32, full) < 5e-3
+    ops.check_errors()
