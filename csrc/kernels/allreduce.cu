@@ -167,6 +167,146 @@ __global__ void __launch_bounds__(THREADS) allreduce_kernel(const Args a) {
   if (threadIdx.x == 0) a.epochs[blockIdx.x] = s_e;
 }
 
+// ---------------------------------------------------------------------------------------
+// Fused variant for the row-parallel output of a transformer sub-layer:
+//   x <- x + allreduce(y);  h <- rmsnorm(x) * w
+// with the rounding of the unfused path (sum in fp32 -> bf16, add -> bf16, norm in fp32).
+// Rows are owned in contiguous ranges (rank j owns rows [j * rp, (j + 1) * rp)); the owner
+// reduces a row, updates its residual, pushes the new residual row to every peer (recv2)
+// and normalises it; the other ranks poll the row, update their residual copy and
+// normalise it too.  CTA b takes rows b, b + G, ... on every rank, so a wait only ever
+// targets the same CTA slot on another rank for the same row, whose own inputs come from
+// the push phase every CTA finishes first: no cycle.  The grid (and so every CTA's epoch) is
+// the same as the plain kernel's, with which it shares the receive buffers.
+// ---------------------------------------------------------------------------------------
+constexpr int MAX_VPT = 4;   // hidden <= 8 * THREADS * MAX_VPT = 8192
+
+struct NormArgs {
+  Args b;                // in = partial [T * HV]; out unused
+  uint4* x;              // residual [T * HV], updated in place
+  const uint4* w;        // norm weight [HV]
+  uint4* h;              // normalised output [T * HV]
+  int T, HV;
+  float eps;
+};
+
+__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+__global__ void __launch_bounds__(THREADS) allreduce_rmsnorm_kernel(const NormArgs na) {
+  const Args& a = na.b;
+  __shared__ int s_e;
+  __shared__ float red[THREADS / 32];
+  if (threadIdx.x == 0) s_e = a.epochs[blockIdx.x] + 1;
+  __syncthreads();
+  const uint64_t t0 = globaltimer_ns();
+  const int par = s_e & 1;
+  const int W = a.world, me = a.rank;
+  const int rp = (na.T + W - 1) / W;
+  const int64_t per = static_cast<int64_t>(rp) * na.HV;
+  const int64_t step = static_cast<int64_t>(gridDim.x) * THREADS;
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * THREADS + threadIdx.x;
+  const uint4 sent = make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu);
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+  bool ok = true;
+
+  // ---- push: rows of owner j -> rank j's recv1[par][me] ----
+  for (int d = 1; d < W; ++d) {
+    const int j = (me + d) % W;
+    const int64_t lo = j * per, hi = min(a.nvec, lo + per);
+    uint4* dst = a.recv1[j] + (static_cast<int64_t>(par) * W + me) * a.max_per - lo;
+#pragma unroll 4
+    for (int64_t v = lo + first; v < hi; v += step) dst[v] = canon4(a.in[v]);
+  }
+  // ---- rows b, b + G, ...: reduce (owner) or receive, then residual update and norm ----
+  const int64_t my_lo = me * per;
+  uint4* r1 = a.recv1[me] + static_cast<int64_t>(par) * W * a.max_per;
+  uint4* r2 = a.recv2[me] + static_cast<int64_t>(par) * a.max_vec;
+  for (int r = blockIdx.x; r < na.T; r += gridDim.x) {
+    const bool own = r / rp == me;
+    float xv[MAX_VPT][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAX_VPT; ++i) {
+      const int vi = threadIdx.x + i * THREADS;
+      if (vi >= na.HV) continue;
+      const int64_t v = static_cast<int64_t>(r) * na.HV + vi;
+      uint4 xn;
+      if (own) {
+        float acc[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+        for (int s2 = 0; s2 < W; ++s2) {
+          uint4 q = zero;
+          if (s2 == me) {
+            q = a.in[v];
+          } else if (ok) {
+            uint4* p = r1 + s2 * a.max_per + (v - my_lo);
+            if (poll(p, q, t0)) *p = sent;
+            else { ok = false; q = zero; }
+          }
+          add8(acc, q);
+        }
+        float xr[8];
+        unpack8(na.x[v], xr);
+        uint32_t* xw = reinterpret_cast<uint32_t*>(&xn);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float y0 = __bfloat162float(__float2bfloat16(acc[2 * k]));
+          const float y1 = __bfloat162float(__float2bfloat16(acc[2 * k + 1]));
+          xw[k] = pack_bf16x2(xr[2 * k] + y0, xr[2 * k + 1] + y1);
+        }
+        const uint4 o = canon4(xn);
+        for (int d = 1; d < W; ++d) {
+          const int j = (me + d) % W;
+          a.recv2[j][static_cast<int64_t>(par) * a.max_vec + v] = o;
+        }
+      } else {
+        xn = zero;
+        if (ok) {
+          if (poll(r2 + v, xn, t0)) r2[v] = sent;
+          else { ok = false; xn = zero; }
+        }
+      }
+      na.x[v] = xn;
+      unpack8(xn, xv[i]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) ss += xv[i][k] * xv[i][k];
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int k = 0; k < THREADS / 32; ++k) tot += red[k];
+    const float inv = rsqrtf(tot / (8.f * na.HV) + na.eps);
+    __syncthreads();   // red is rewritten by the next row
+#pragma unroll
+    for (int i = 0; i < MAX_VPT; ++i) {
+      const int vi = threadIdx.x + i * THREADS;
+      if (vi >= na.HV) continue;
+      float wf[8];
+      unpack8(na.w[vi], wf);
+      uint4 o;
+      uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        ow[k] = pack_bf16x2(xv[i][2 * k] * inv * wf[2 * k], xv[i][2 * k + 1] * inv * wf[2 * k + 1]);
+      na.h[static_cast<int64_t>(r) * na.HV + vi] = o;
+    }
+  }
+  if (!ok) record_error(a.err, kErrTimeoutPeer);
+  __syncthreads();
+  if (threadIdx.x == 0) a.epochs[blockIdx.x] = s_e;
+}
+
 struct Layout {
   int64_t max_vec, max_per, recv1_off, recv2_off, bytes;
 };
@@ -229,6 +369,52 @@ void allreduce_p2p(at::Tensor& out, const at::Tensor& inp, std::vector<int64_t> 
   const int g = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ctas, ar::MAX_CTAS)));
   ar::allreduce_kernel<<<g, ar::THREADS, 0, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// h = rmsnorm(x + allreduce(inp)) * w, x updated in place; all [T, H] bf16 contiguous.
+// Returns false (nothing launched) when a row-owner slice would not fit the receive buffers.
+bool allreduce_rmsnorm_p2p(at::Tensor& h, const at::Tensor& inp, at::Tensor& x,
+                           const at::Tensor& w, std::vector<int64_t> bases, int64_t rank,
+                           int64_t max_elems, int64_t ctas, double eps, at::Tensor& err) {
+  const int world = static_cast<int>(bases.size());
+  TORCH_CHECK(world >= 2 && world <= ar::MAX_WORLD, "allreduce_rmsnorm_p2p: 2..8 ranks");
+  TORCH_CHECK(inp.dim() == 2 && x.sizes() == inp.sizes() && h.sizes() == inp.sizes(),
+              "allreduce_rmsnorm_p2p: [T, H] shapes");
+  const int64_t T = inp.size(0), H = inp.size(1);
+  for (const at::Tensor& t : {std::cref(h), std::cref(inp), std::cref(x), std::cref(w)})
+    TORCH_CHECK(t.is_contiguous() && t.scalar_type() == at::kBFloat16 &&
+                    reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0,
+                "allreduce_rmsnorm_p2p: contiguous 16-byte-aligned bf16 tensors");
+  TORCH_CHECK(w.numel() == H && H % 8 == 0, "allreduce_rmsnorm_p2p: norm weight / hidden");
+  if (H / 8 > ar::THREADS * ar::MAX_VPT || T * H > max_elems) return false;
+  const ar::Layout l = ar::layout(max_elems, world);
+  const int64_t rp = (T + world - 1) / world;
+  if (rp * (H / 8) > l.max_per) return false;
+  if (T == 0) return true;
+  ar::NormArgs na = {};
+  for (int r = 0; r < world; ++r) {
+    uint8_t* b = reinterpret_cast<uint8_t*>(bases[r]);
+    na.b.recv1[r] = reinterpret_cast<uint4*>(b + l.recv1_off);
+    na.b.recv2[r] = reinterpret_cast<uint4*>(b + l.recv2_off);
+  }
+  na.b.in = reinterpret_cast<const uint4*>(inp.data_ptr());
+  na.b.epochs = reinterpret_cast<int*>(bases[rank]);
+  na.b.nvec = T * H / 8;
+  na.b.max_per = l.max_per;
+  na.b.max_vec = l.max_vec;
+  na.b.world = world;
+  na.b.rank = static_cast<int>(rank);
+  na.b.err = err.data_ptr<int>();
+  na.x = reinterpret_cast<uint4*>(x.data_ptr());
+  na.w = reinterpret_cast<const uint4*>(w.data_ptr());
+  na.h = reinterpret_cast<uint4*>(h.data_ptr());
+  na.T = static_cast<int>(T);
+  na.HV = static_cast<int>(H / 8);
+  na.eps = static_cast<float>(eps);
+  const int g = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ctas, ar::MAX_CTAS)));
+  ar::allreduce_rmsnorm_kernel<<<g, ar::THREADS, 0, at::cuda::getCurrentCUDAStream()>>>(na);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return true;
 }
 
 }  // namespace lb

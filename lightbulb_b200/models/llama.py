@@ -196,19 +196,21 @@ class LlamaModel:
                                     cu_q_cpu=b.cu_q_cpu, scale=self.scale)
             if self.h2o is not None and nd > 0 and i == len(self.layers) - 1 and last:
                 self.h2o.accumulate(q[:nd], kv.k[i], b.block_tables[:nd], b.seq_lens[:nd])
-            o = comm.gemm_all_reduce(attn, L["o"]) if comm is not None else \
-                ops.gemm(attn, L["o"])
-            h = ops.rmsnorm(o, L["ln_post"], eps, residual=x)
+            if comm is not None:
+                h = comm.gemm_all_reduce_rmsnorm(attn, L["o"], x, L["ln_post"], eps)
+            else:
+                h = ops.rmsnorm(ops.gemm(attn, L["o"]), L["ln_post"], eps, residual=x)
             act = ops.gemm(h, L["gate_up"], mode=ops.EPI_SWIGLU)
-            dn = comm.gemm_all_reduce(act, L["down"]) if comm is not None else \
-                ops.gemm(act, L["down"])
             if i + 1 < len(self.layers):
                 nw = self.layers[i + 1]["ln_in"]
             elif last:
                 nw = self.w["norm"]
             else:
                 nw = self._ones(x.shape[1])  # stage boundary: only the residual update matters
-            h = ops.rmsnorm(dn, nw, eps, residual=x)
+            if comm is not None:
+                h = comm.gemm_all_reduce_rmsnorm(act, L["down"], x, nw, eps)
+            else:
+                h = ops.rmsnorm(ops.gemm(act, L["down"]), nw, eps, residual=x)
         if not last:
             return x
         hl = h.index_select(0, b.logits_idx) if b.logits_idx.numel() != T else h

@@ -13,7 +13,7 @@ summed by its owner in rank order, then copied).
 """
 from __future__ import annotations
 
-from typing import List
+from typing import List, Optional
 
 import torch
 import torch.distributed as dist
@@ -61,6 +61,18 @@ class P2PAllReduce:
         self.calls += 1
         return out
 
+    def allreduce_rmsnorm(self, y: torch.Tensor, residual: torch.Tensor, w: torch.Tensor,
+                          eps: float) -> Optional[torch.Tensor]:
+        """``residual += allreduce(y)``; returns ``rmsnorm(residual) * w`` in one launch, or
+        None when the shape does not fit the receive buffers (the caller then composes)."""
+        h = torch.empty_like(y)
+        if not self.C.allreduce_rmsnorm_p2p(h, y, residual, w, self.bases, self.rank,
+                                            self.max_elems, self.ctas, float(eps), self.err):
+            return None
+        ops.launch_counter_add(1)
+        self.calls += 1
+        return h
+
     def close(self):
         for r, b in enumerate(self.bases):
             if r != self.rank:
@@ -99,6 +111,32 @@ def selfcheck(argv=None) -> int:
         tol = 0.01 * ref[fin].abs().max().item() + 1e-2
         if err > tol or bool(torch.isnan(y.float()[~fin]).logical_not().any()):
             bad.append((n, err, tol))
+    # fused residual add + RMSNorm, interleaved with plain calls (shared per-CTA epochs)
+    for T, H in [(1, 4096), (3, 4096), (256, 4096), (255, 2048), (2, 8192), (129, 4096)]:
+        y = (torch.randn(T, H, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+        x0 = torch.randn(T, H, device=dev, generator=torch.Generator(device=dev).manual_seed(7))
+        x0 = x0.to(torch.bfloat16)
+        wn = (1 + 0.1 * torch.randn(H, device=dev,
+                                    generator=torch.Generator(device=dev).manual_seed(8)))
+        wn = wn.to(torch.bfloat16)
+        x = x0.clone()
+        h = ar.allreduce_rmsnorm(y, x, wn, 1e-5)
+        if h is None:
+            bad.append((T, H, "not launched"))
+            continue
+        ar(y.view(-1).clone())                 # a plain call in between
+        parts = [torch.empty_like(y) for _ in range(world)]
+        dist.all_gather(parts, y)
+        ysum = torch.stack([p.float() for p in parts]).sum(0).to(torch.bfloat16).float()
+        xr = (x0.float() + ysum).to(torch.bfloat16).float()
+        hr = xr * torch.rsqrt(xr.pow(2).mean(-1, keepdim=True) + 1e-5) * wn.float()
+        if (x.float() - xr).abs().max().item() > 0.02 * xr.abs().max().item() + 1e-2 or \
+                ((h.float() - hr).norm() / hr.norm()).item() > 1e-2:
+            bad.append((T, H, "fused mismatch"))
+        hs = [torch.empty_like(h) for _ in range(world)]
+        dist.all_gather(hs, h)
+        if not all(torch.equal(hs[0].view(torch.int16), t.view(torch.int16)) for t in hs):
+            bad.append((T, H, "fused ranks differ"))
     ops.check_errors(dev)
     torch.cuda.synchronize()
     if rank == 0:

@@ -74,6 +74,19 @@ class TPComm:
             return ar(x)
         return self.all_reduce(ops.gemm(a, w))
 
+    def gemm_all_reduce_rmsnorm(self, a: torch.Tensor, w, residual: torch.Tensor,
+                                norm_w: torch.Tensor, eps: float) -> torch.Tensor:
+        """Row-parallel layer followed by the residual add and RMSNorm:
+        ``residual += sum_ranks(a @ w.T)``; returns ``rmsnorm(residual) * norm_w``.  With the
+        peer-memory all-reduce the sum, the add and the norm are one kernel."""
+        ar = self.p2p_ar
+        m, n = a.shape[0], w.shape[0]
+        if ar is not None and a.is_cuda and ar.fits(m * n):
+            h = ar.allreduce_rmsnorm(ops.gemm(a, w), residual, norm_w, eps)
+            if h is not None:
+                return h
+        return ops.rmsnorm(self.gemm_all_reduce(a, w), norm_w, eps, residual=residual)
+
     def close(self):
         if self.p2p_ar is not None:
             torch.cuda.synchronize()

@@ -103,6 +103,14 @@ def main(argv=None) -> int:
         ops.gemm(hh, Wgu, mode=ops.EPI_SWIGLU)
 
     res["p2p_chain_us"] = timed(p2p_chain)
+    xr = x.clone()
+    res["p2p_allreduce_rmsnorm_us"] = timed(lambda: ar.allreduce_rmsnorm(o, xr, lnw, 1e-5))
+
+    def p2p_norm_chain():
+        hh = comm.gemm_all_reduce_rmsnorm(attn, Wo, xr, lnw, 1e-5)
+        ops.gemm(hh, Wgu, mode=ops.EPI_SWIGLU)
+
+    res["p2p_norm_chain_us"] = timed(p2p_norm_chain)
     o2 = ops.gemm(attn, Wo)               # o itself was all-reduced in place by the timing above
     ref = o2.float().clone()
     dist.all_reduce(ref)
