@@ -49,6 +49,9 @@ class TPComm:
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.fused = None  # set by parallel.fused when peer-memory kernels are enabled
         self.p2p_ar = None  # two-shot peer-memory all-reduce (parallel/allreduce.py)
+        # one-kernel all-reduce + residual + RMSNorm; off by default: measured at TP2 (256 x
+        # 4096) 14.0 us against 8.4 + 4.1 us for the all-reduce and the norm kernel
+        self.fuse_norm = False
 
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         if self.world > 1:
@@ -81,7 +84,7 @@ class TPComm:
         peer-memory all-reduce the sum, the add and the norm are one kernel."""
         ar = self.p2p_ar
         m, n = a.shape[0], w.shape[0]
-        if ar is not None and a.is_cuda and ar.fits(m * n):
+        if self.fuse_norm and ar is not None and a.is_cuda and ar.fits(m * n):
             h = ar.allreduce_rmsnorm(ops.gemm(a, w), residual, norm_w, eps)
             if h is not None:
                 return h
