@@ -22,6 +22,7 @@ class Fact:
     content: str
     source: str = "user"
     confidence: float = 1.0
+    key: Optional[str] = None          # optional name for exact lookup (e.g. "gdp_2023")
     id: str = field(default_factory=lambda: uuid.uuid4().hex[:12])
     created: float = field(default_factory=time.time)
 
@@ -31,11 +32,28 @@ class KnowledgeBase:
         self.facts: List[Fact] = []
         self._lock = threading.Lock()
 
-    def add(self, content: str, source: str = "user", confidence: float = 1.0) -> Fact:
-        f = Fact(content, source, float(confidence))
+    def add(self, content: str, source: str = "user", confidence: float = 1.0,
+            key: Optional[str] = None) -> Fact:
+        f = Fact(content, source, float(confidence), key)
         with self._lock:
             self.facts.append(f)
         return f
+
+    def __deepcopy__(self, memo):
+        """Independent copy (facts cloned, fresh lock): used to explore branches of a plan."""
+        kb = KnowledgeBase()
+        with self._lock:
+            kb.facts = [Fact(f.content, f.source, f.confidence, f.key, f.id, f.created)
+                        for f in self.facts]
+        return kb
+
+    def get(self, key: str) -> Optional[Fact]:
+        """The newest fact stored under ``key`` (exact name), if any."""
+        with self._lock:
+            for f in reversed(self.facts):
+                if f.key == key:
+                    return f
+        return None
 
     def query(self, text: str, top_k: int = 5, min_score: float = 0.0) -> List[dict]:
         q = _toks(text)
