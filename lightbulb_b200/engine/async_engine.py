@@ -59,6 +59,13 @@ class AsyncEngine:
         self._thread = threading.Thread(target=self._loop, name="lb-engine", daemon=True)
         self._thread.start()
 
+    def fail(self, reason: str) -> None:
+        """Orderly stop after an external failure (e.g. a peer rank died): no further steps;
+        every in-flight request finishes with an error; the server reports 503."""
+        self.healthy = False
+        self.last_error = reason
+        self._submit.put(("fail", reason))
+
     # ---- engine thread ----------------------------------------------------------------
     def _loop(self):
         eng = self.engine
@@ -80,6 +87,20 @@ class AsyncEngine:
                 elif kind == "abort":
                     eng.abort(payload)
                     self._streams.pop(payload, None)
+                elif kind == "fail":
+                    for rid in list(self._streams):
+                        self._emit(rid, StreamItem(finished=True, finish_reason="error",
+                                                   error=payload))
+                        eng.abort(rid)
+            if not self.healthy:
+                # failed: keep draining submissions (each fails at once), never step again
+                for rid in list(self._streams):
+                    self._emit(rid, StreamItem(finished=True, finish_reason="error",
+                                               error=self.last_error))
+                    eng.abort(rid)
+                if not drained:
+                    time.sleep(self._idle)
+                continue
             if not eng.has_unfinished():
                 if not drained:
                     time.sleep(self._idle)

@@ -176,6 +176,8 @@ def create_app(state: Optional[AppState] = None) -> FastAPI:
         created = int(time.time())
         cid = f"chatcmpl-{uuid.uuid4()}"
 
+        if state.engine is not None and not state.engine.healthy:
+            return _err(503, f"engine unavailable: {state.engine.last_error}", "unavailable")
         if state.engine is None:
             text = f"Received request for model '{model}'. No model available on the server."
             if stream:
@@ -280,6 +282,8 @@ def create_app(state: Optional[AppState] = None) -> FastAPI:
         prompt_text = "\n".join(p) if isinstance(p, list) else str(p)
         model = body.get("model", state.model_name)
         created = int(time.time())
+        if state.engine is not None and not state.engine.healthy:
+            return _err(503, f"engine unavailable: {state.engine.last_error}", "unavailable")
         if state.engine is None:
             return {"id": f"cmpl-{uuid.uuid4()}", "object": "text_completion", "created": created,
                     "model": model, "choices": [{"text": "No model available on the server.",
