@@ -59,6 +59,20 @@ class AsyncEngine:
         self._thread = threading.Thread(target=self._loop, name="lb-engine", daemon=True)
         self._thread.start()
 
+    def call(self, fn):
+        """Run ``fn(engine)`` on the engine thread between steps; returns a
+        ``concurrent.futures.Future`` (``asyncio.wrap_future`` it from coroutines)."""
+        import concurrent.futures
+        fut = concurrent.futures.Future()
+        self._submit.put(("call", (fn, fut)))
+        return fut
+
+    def _emit_outputs(self, outs) -> None:
+        for o in outs:
+            self._emit(o.request_id, StreamItem(o.new_text, o.new_token_ids, o.finished,
+                                                o.finish_reason, o.prompt_tokens,
+                                                o.completion_tokens, o.cached_tokens))
+
     def fail(self, reason: str) -> None:
         """Orderly stop after an external failure (e.g. a peer rank died): no further steps;
         every in-flight request finishes with an error; the server reports 503."""
@@ -87,6 +101,15 @@ class AsyncEngine:
                 elif kind == "abort":
                     eng.abort(payload)
                     self._streams.pop(payload, None)
+                elif kind == "call":
+                    fn, fut = payload
+                    try:
+                        res = fn(eng)
+                        if isinstance(res, dict) and "drained" in res:
+                            self._emit_outputs(res.pop("drained"))
+                        fut.set_result(res)
+                    except Exception as e:
+                        fut.set_exception(e)
                 elif kind == "fail":
                     for rid in list(self._streams):
                         self._emit(rid, StreamItem(finished=True, finish_reason="error",
@@ -116,10 +139,7 @@ class AsyncEngine:
                     self._emit(rid, StreamItem(finished=True, finish_reason="error", error=repr(e)))
                     eng.abort(rid)
                 continue
-            for o in outs:
-                self._emit(o.request_id, StreamItem(o.new_text, o.new_token_ids, o.finished,
-                                                    o.finish_reason, o.prompt_tokens,
-                                                    o.completion_tokens, o.cached_tokens))
+            self._emit_outputs(outs)
 
     def _emit(self, rid: str, item: StreamItem):
         st = self._streams.get(rid)

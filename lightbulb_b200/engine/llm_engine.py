@@ -314,6 +314,11 @@ class LLMEngine:
             return []
         return self._collect(prev)
 
+    def drain(self) -> List[RequestOutput]:
+        """Finish an overlapped decode step still in flight and return its outputs (the engine
+        is then quiescent: every sequence's tokens are on the host)."""
+        return self._collect_pending()
+
     def _collect_pending(self) -> List[RequestOutput]:
         p, self._pending = self._pending, None
         return self._collect(p) if p is not None else []

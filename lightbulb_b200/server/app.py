@@ -20,6 +20,7 @@ Unlike the reference, many concurrent requests share one continuous batch
 """
 from __future__ import annotations
 
+import asyncio
 import json
 import logging
 import os
@@ -36,7 +37,8 @@ from ..engine.eos_monitor import EosMonitor
 from ..engine.sampling import SamplingParams
 from ..extras.knowledge import KnowledgeBase
 from ..extras.reasoning import ReasoningControls
-from ..extras.state import CheckpointManager, engine_snapshot
+from ..extras.state import (CheckpointManager, engine_snapshot, restore_engine_state,
+                             save_engine_state)
 from ..extras.tools import ToolRegistry
 from ..templates.chat_template import BuiltPrompt, ResolvedTemplate, legacy_join
 from .auth import AuthStore
@@ -396,7 +398,15 @@ def create_app(state: Optional[AppState] = None) -> FastAPI:
         e = _eng()
         payload = engine_snapshot(e) if e is not None else {"requests": []}
         payload["knowledge"] = [f.__dict__ for f in state.kb.facts]
-        return state.ckpt.save(b.get("name") or f"ckpt-{int(time.time())}", payload)
+        name = b.get("name") or f"ckpt-{int(time.time())}"
+        res = state.ckpt.save(name, payload)
+        if b.get("include_kv") and state.engine is not None:
+            # requests + KV rows of their cached positions, written on the engine thread
+            path = state.ckpt.kv_path(name)
+            info = await asyncio.wrap_future(state.engine.call(
+                lambda eng: save_engine_state(eng, path)))
+            res = dict(res, kv=info)
+        return res
 
     @app.post("/v1/lightbulb/state/restore")
     async def state_restore(request: Request):
@@ -407,7 +417,16 @@ def create_app(state: Optional[AppState] = None) -> FastAPI:
             return _err(404, f"no checkpoint: {ex}")
         for f in m["payload"].get("knowledge", []):
             state.kb.add(f.get("content", ""), f.get("source", "user"), f.get("confidence", 1.0))
-        return {"restored": m["name"], "requests": len(m["payload"].get("requests", []))}
+        out = {"restored": m["name"], "requests": len(m["payload"].get("requests", []))}
+        path = state.ckpt.kv_path(m["name"])
+        if b.get("kv") and state.engine is not None and os.path.exists(path):
+            try:
+                ids = await asyncio.wrap_future(state.engine.call(
+                    lambda eng: restore_engine_state(eng, path)))
+            except ValueError as ex:
+                return _err(409, str(ex))
+            out["resumed"] = ids
+        return out
 
     @app.post("/v1/lightbulb/state/branch")
     async def state_branch(request: Request):
