@@ -52,6 +52,8 @@ struct AttnArgs {
   float* part_lse;      // [splits, T*Hq]
   int total_rows;       // T * Hq
   int causal;
+  int num_blocks;       // KV pool size: block ids outside [0, num_blocks) are rejected
+  int* err;             // error word (nullptr: not reported)
 };
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
@@ -99,9 +101,15 @@ __device__ __forceinline__ void load_kv_tile(bf16* sK, bf16* sV, const AttnArgs&
     const int idx = threadIdx.x + i * ATHREADS;
     const int r = idx >> 4, c = idx & 15;
     const int key = kbase + r;
-    const bool ok = key < kv_len;
+    bool ok = key < kv_len;
     const int kk = ok ? key : 0;
-    const int blk = btab[kk / a.block_size];
+    int blk = btab[kk / a.block_size];
+    if (static_cast<unsigned>(blk) >= static_cast<unsigned>(a.num_blocks)) {
+      // corrupt block table: report, read nothing (the key is zero-filled and masked)
+      if (ok && a.err != nullptr) record_error(a.err, kErrBounds);
+      blk = 0;
+      ok = false;
+    }
     const size_t off = ((static_cast<size_t>(blk) * a.num_kv_heads + kvh) * a.block_size +
                         (kk % a.block_size)) * AD + c * 8;
     cp_async16(sK + swz(r, c), a.k_cache + off, ok);
@@ -412,7 +420,8 @@ void paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::T
                      const at::Tensor& cu_q, const c10::optional<at::Tensor>& tile_seq,
                      const c10::optional<at::Tensor>& tile_row0, int64_t group, double scale,
                      bool decode, int64_t num_splits, const c10::optional<at::Tensor>& part_o,
-                     const c10::optional<at::Tensor>& part_lse, bool causal) {
+                     const c10::optional<at::Tensor>& part_lse, bool causal,
+                     const c10::optional<at::Tensor>& err) {
   TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k_cache.scalar_type() == at::kBFloat16,
               "paged_attention: bf16 q / cache");
   TORCH_CHECK(q.dim() == 3 && q.size(2) == AD && q.stride(2) == 1 && q.stride(1) == AD,
@@ -443,6 +452,8 @@ void paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::T
   a.total_rows = q.size(0) * q.size(1);
   a.tile_seq = nullptr;
   a.tile_row0 = nullptr;
+  a.num_blocks = static_cast<int>(k_cache.size(0));
+  a.err = (err.has_value() && err->defined()) ? err->data_ptr<int>() : nullptr;
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   if (decode) {
     TORCH_CHECK(group <= AROWS, "decode path packs <= 16 rows per KV head");

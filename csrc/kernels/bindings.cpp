@@ -12,7 +12,8 @@ void paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::T
                      const at::Tensor& cu_q, const c10::optional<at::Tensor>& tile_seq,
                      const c10::optional<at::Tensor>& tile_row0, int64_t group, double scale,
                      bool decode, int64_t num_splits, const c10::optional<at::Tensor>& part_o,
-                     const c10::optional<at::Tensor>& part_lse, bool causal);
+                     const c10::optional<at::Tensor>& part_lse, bool causal,
+                     const c10::optional<at::Tensor>& err);
 void paged_decode_tma(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                       at::Tensor& out, const at::Tensor& block_tables, const at::Tensor& seq_lens,
                       int64_t group, double scale, int64_t num_splits,
@@ -73,7 +74,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("ws"), py::arg("counters"), py::arg("err"), py::arg("bt"), py::arg("splits"),
         py::arg("trace") = py::none());
   m.def("gemm_plan", &lb::gemm_plan, "token tile, split-K and workspace size of a GEMM");
-  m.def("paged_attention", &lb::paged_attention, "paged attention (decode / prefill)");
+  m.def("paged_attention", &lb::paged_attention, "paged attention (decode / prefill)",
+        py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("out"),
+        py::arg("block_tables"), py::arg("seq_lens"), py::arg("cu_q"), py::arg("tile_seq"),
+        py::arg("tile_row0"), py::arg("group"), py::arg("scale"), py::arg("decode"),
+        py::arg("num_splits"), py::arg("part_o"), py::arg("part_lse"), py::arg("causal"),
+        py::arg("err") = py::none());
   m.def("paged_decode_tma", &lb::paged_decode_tma, "TMA-fed warp-specialised paged decode");
   m.def("gemm_bf16_tp", &lb::gemm_bf16_tp, "tensor-parallel GEMM (wait / scatter / signal)",
         py::arg("A"), py::arg("W"), py::arg("C"), py::arg("mode"), py::arg("err"),

@@ -327,7 +327,8 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
             _launches[0] += 2 if num_splits > 1 else 1
             return out
         C.paged_attention(q, k_cache, v_cache, out, block_tables, seq_lens, cu_q, tile_seq,
-                          tile_row0, group, scale, decode, num_splits, po, pl, causal)
+                          tile_row0, group, scale, decode, num_splits, po, pl, causal,
+                          scratch(q.device).err)
         _launches[0] += 2 if (decode and num_splits > 1) else 1
         return out
     # CPU restatement

@@ -3,9 +3,10 @@
 Every rank runs two host threads: a beat thread that increments the rank's counter in the
 store every ``interval_s``, and a monitor that reads every peer's counter and records, on its
 own monotonic clock, when each one last changed.  A peer whose counter has not moved for
-``timeout_s`` is declared failed (no clock agreement between hosts is needed); a store that
-stops answering (its host rank died) counts as a failure too.  ``on_failure`` is called once,
-from the monitor thread, with the set of failed ranks; :func:`attach` connects it to an
+``timeout_s`` is declared failed (no clock agreement between hosts is needed); a peer that
+has never beaten is only declared failed after ``startup_timeout_s`` (ranks start at different
+times); a store that stops answering (its host rank died) counts as a failure too.
+``on_failure`` is called once, from the monitor thread, with the set of failed ranks; :func:`attach` connects it to an
 :class:`~lightbulb_b200.engine.async_engine.AsyncEngine`, which then stops stepping, fails
 its in-flight requests and makes the server answer 503.
 
@@ -25,11 +26,12 @@ STORE_FAILURE = -1       # pseudo-rank reported when the store itself is unreach
 class Watchdog:
     def __init__(self, store, rank: int, world: int, interval_s: float = 0.5,
                  timeout_s: float = 5.0, on_failure: Optional[Callable[[Set[int]], None]] = None,
-                 prefix: str = "lb_hb"):
+                 prefix: str = "lb_hb", startup_timeout_s: float = 120.0):
         if timeout_s <= 2 * interval_s:
             raise ValueError("timeout_s must exceed two heartbeat intervals")
         self.store, self.rank, self.world = store, rank, world
         self.interval, self.timeout = interval_s, timeout_s
+        self.startup_timeout = max(startup_timeout_s, timeout_s)
         self.on_failure = on_failure
         self.prefix = prefix
         self.failed: Set[int] = set()
@@ -66,13 +68,17 @@ class Watchdog:
                 except Exception:
                     dead.add(STORE_FAILURE)
                     break
+                if c == 0:
+                    # never beaten yet: ranks start at different times, so a peer is timed
+                    # only after its first beat, and otherwise gets the (longer) startup limit
+                    if now - start > self.startup_timeout:
+                        dead.add(r)
+                    continue
                 prev = self._seen.get(r)
                 if prev is None or prev[0] != c:
                     self._seen[r] = (c, now)
                 elif now - prev[1] > self.timeout:
                     dead.add(r)
-            if not self._seen and now - start > self.timeout:
-                dead.update(r for r in range(self.world) if r != self.rank)
             if dead:
                 self._declare(dead)
             self._stop.wait(self.interval)

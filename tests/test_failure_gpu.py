@@ -40,3 +40,39 @@ def test_allreduce_peer_never_signals_reports_timeout():
     ref = a.float() @ w.float().T
     assert ((ops.gemm(a, w).float() - ref).norm() / ref.norm()).item() < 1e-2
     ops.check_errors(dev)
+
+
+@pytest.mark.parametrize("decode", [True, False])
+@pytest.mark.parametrize("bad", [10_000, -7])
+def test_corrupt_block_table_is_reported_not_faulted(decode, bad):
+    # an out-of-range block id (a corrupted table) must be reported through the error word;
+    # the kernel reads no memory outside the KV pool and the context stays usable
+    from test_kernels_gpu import _paged_setup, _rel, _ref_paged
+    from lightbulb_b200.models.llama import prefill_tiles
+    dev = torch.device("cuda", 0)
+    seq_lens = [40, 300, 17]
+    q_lens = [1, 1, 1] if decode else [40, 20, 17]
+    q, kc, vc, bt, sl, cu = _paged_setup(seq_lens, q_lens, 8, 2, seed=5)
+    bt_bad = bt.clone()
+    bt_bad[1, 3] = bad                               # sequence 1, its 4th block
+    kw = {}
+    if not decode:
+        ts, tr = prefill_tiles(cu.tolist(), 0, 4)
+        kw = dict(tile_seq=torch.tensor(ts, dtype=torch.int32, device=dev),
+                  tile_row0=torch.tensor(tr, dtype=torch.int32, device=dev))
+    out = torch.empty(q.shape, dtype=torch.bfloat16, device=dev)
+    ops.scratch(dev).err.zero_()
+    ops.paged_attention(q.to(dev), kc.to(dev), vc.to(dev), bt_bad.to(dev), sl.to(dev),
+                        cu.to(dev), out, 4, decode=decode, **kw)
+    torch.cuda.synchronize()
+    with pytest.raises(ops.KernelError, match="index out of bounds"):
+        ops.check_errors(dev)
+    # the untouched sequences are still exact, and a clean call reports nothing
+    ref = _ref_paged(q, kc, vc, bt, sl, cu)
+    r0 = slice(int(cu[0]), int(cu[1]))
+    assert _rel(out[r0].cpu(), ref[r0]) < 2e-2
+    ops.paged_attention(q.to(dev), kc.to(dev), vc.to(dev), bt.to(dev), sl.to(dev), cu.to(dev),
+                        out, 4, decode=decode, **kw)
+    torch.cuda.synchronize()
+    ops.check_errors(dev)
+    assert _rel(out.cpu(), ref) < 2e-2

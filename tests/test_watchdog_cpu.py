@@ -26,8 +26,10 @@ def _rank(rank, world, port, scenario, q):
     import torch.distributed as dist
     store = dist.TCPStore("127.0.0.1", port, world, rank == 0,
                           timeout=datetime.timedelta(seconds=20), wait_for_workers=False)
+    store.set(f"ready/{rank}", "1")                 # start together: spawn times differ
+    store.wait([f"ready/{r}" for r in range(world)], datetime.timedelta(seconds=60))
     seen = []
-    wd = Watchdog(store, rank, world, interval_s=0.1, timeout_s=1.0,
+    wd = Watchdog(store, rank, world, interval_s=0.1, timeout_s=1.0, startup_timeout_s=30.0,
                   on_failure=lambda dead: seen.append((sorted(dead), time.monotonic())))
     wd.start()
     t0 = time.monotonic()
@@ -70,7 +72,7 @@ def test_rank_exit_is_detected_by_every_survivor():
     for r in (0, 1):
         dead, t = out[r]
         assert dead == [2], out
-        assert 1.0 <= t <= 3.0, out
+        assert 1.0 <= t <= 6.0, out
 
 
 def test_silent_rank_is_detected():
@@ -82,6 +84,24 @@ def test_silent_rank_is_detected():
 def test_no_failure_no_report():
     out = _run("none")
     assert all(v[0] == [] for v in out.values()), out
+
+
+def test_peer_that_never_starts_uses_startup_limit():
+    class Store:
+        def __init__(self):
+            self.d = {}
+
+        def add(self, k, v):
+            self.d[k] = self.d.get(k, 0) + v
+            return self.d[k]
+    got = []
+    wd = Watchdog(Store(), 0, 2, interval_s=0.05, timeout_s=0.2, startup_timeout_s=0.8,
+                  on_failure=got.append).start()
+    time.sleep(0.5)
+    assert not got                       # not yet: the peer may still be starting
+    time.sleep(0.8)
+    wd.stop()
+    assert got and got[0] == {1}
 
 
 def test_unreachable_store_counts_as_failure():
@@ -119,7 +139,8 @@ def test_engine_fail_stops_requests_and_server_503():
         def add(self, k, v):
             self.d[k] = self.d.get(k, 0) + v
             return self.d[k]
-    wd = attach(ae, Watchdog(Store(), 0, 2, interval_s=0.05, timeout_s=0.3))
+    wd = attach(ae, Watchdog(Store(), 0, 2, interval_s=0.05, timeout_s=0.3,
+                             startup_timeout_s=0.3))
 
     async def scenario():
         items = []
