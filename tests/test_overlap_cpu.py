@@ -98,3 +98,50 @@ def test_overlap_stop_token_mid_stream():
     b, n_b = _run(True, prompts, params)
     assert n_b > 0 and a == b
     assert a[0][1] == "stop" and a[0][0][-1] == stop and len(a[0][0]) <= 6
+
+
+def test_overlap_abort_mid_stream_and_stop_strings():
+    # abort a request while its newest id is still pending, and finish another on a text stop
+    # string: the other requests must match the synchronous engine and every block be freed
+    prompts = [[21, 22, 23], [31, 32, 33, 34], [41] * 12]
+    sp = [SamplingParams(temperature=0.0, max_tokens=40, ignore_eos=True) for _ in prompts]
+    ref, _ = _run(False, prompts, sp)
+    stop_text = None
+
+    def go(overlap):
+        eng = _engine(overlap)
+        seqs = [eng.add_request(f"r{i}", prompt_token_ids=p, params=s)
+                for i, (p, s) in enumerate(zip(prompts, sp))]
+        for _ in range(10):
+            eng.step()
+        eng.abort("r1")
+        while eng.has_unfinished():
+            eng.step()
+        eng.blocks.check_invariants()
+        assert eng.blocks.num_free_blocks() == 96
+        return [(s.output_token_ids, s.finish_reason) for s in seqs]
+
+    a, b = go(False), go(True)
+    assert a[0] == b[0] == ref[0] and a[2] == b[2] == ref[2]
+    assert a[1][1] == b[1][1] == "abort"
+    assert PENDING_TOKEN not in b[1][0] and b[1][0] == ref[1][0][:len(b[1][0])]
+
+    # stop string: take a piece of the greedy text of request 0 and stop on it
+    eng = _engine(False)
+    s0 = eng.add_request("t", prompt_token_ids=prompts[0], params=SamplingParams(
+        temperature=0.0, max_tokens=40, ignore_eos=True))
+    while eng.has_unfinished():
+        eng.step()
+    text = s0.output_text
+    if len(text) >= 8:
+        stop_text = text[4:8]
+        outs = []
+        for overlap in (False, True):
+            e = _engine(overlap)
+            s = e.add_request("t", prompt_token_ids=prompts[0], params=SamplingParams(
+                temperature=0.0, max_tokens=40, ignore_eos=True, stop=[stop_text]))
+            while e.has_unfinished():
+                e.step()
+            outs.append((s.output_token_ids, s.output_text, s.finish_reason))
+            e.blocks.check_invariants()
+        assert outs[0] == outs[1] and outs[0][2] == "stop"
