@@ -43,7 +43,7 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-BASELINE_TOKS = None  # BASELINE.md publishes no number for this config
+BASELINE_TOKS = None  # the reference publishes no B200 figure for this metric and config
 
 
 def parse():
@@ -173,7 +173,7 @@ def reference_arm(args):
     line = {"impl": "reference",
             "unavailable": "ciresnave/lightbulb is a Rust crate (cargo/rustc absent from the image, "
                            "git dependencies candlelight/fuel need network, CI documents Linux "
-                           "builds failing); pip install of /root/reference fails: no setup.py "
+                           "builds failing); pip install of the reference source fails: no setup.py "
                            "or pyproject.toml"}
     rank = int(os.environ.get("RANK", "0"))
     if rank == 0:
