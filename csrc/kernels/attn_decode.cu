@@ -53,7 +53,6 @@ struct Args {
   float* part_o;
   float* part_lse;
   int total_rows;
-  int num_blocks;       // KV pool size: block ids outside [0, num_blocks) are reported
   int* err;
 };
 
@@ -158,11 +157,9 @@ __global__ void __launch_bounds__(THREADS, 2)
         uint8_t* sK = sKV + stage * STAGE_BYTES;
         uint8_t* sV = sK + TILE_BYTES;
         for (int b = 0; b < KT / BS; ++b) {
-          int blk = btab[(kb >> 4) + (b < nblk ? b : 0)];
-          if (static_cast<unsigned>(blk) >= static_cast<unsigned>(a.num_blocks)) {
-            record_error(a.err, kErrBounds);   // corrupt block table: load block 0 instead
-            blk = 0;
-          }
+          // A block id outside the pool gives a row coordinate outside the tensor map, which
+          // the TMA zero-fills: a corrupted table cannot read outside the KV pool here.
+          const int blk = btab[(kb >> 4) + (b < nblk ? b : 0)];
           const int row = (blk * a.num_kv_heads + kvh) * BS;
           for (int h = 0; h < 2; ++h) {
             tma_load_2d(sK + h * HALF_BYTES + b * BS * 128, &tmK, &full[stage], h * 64, row, pol);
@@ -378,7 +375,6 @@ void paged_decode_tma(const at::Tensor& q, const at::Tensor& k_cache, const at::
   a.part_lse = nullptr;
   a.total_rows = q.size(0) * q.size(1);
   a.err = err.data_ptr<int>();
-  a.num_blocks = static_cast<int>(k_cache.size(0));
   if (a.num_splits > 1) {
     TORCH_CHECK(part_o.has_value() && part_lse.has_value(), "split-KV needs workspaces");
     a.part_o = part_o->data_ptr<float>();
