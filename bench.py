@@ -29,6 +29,11 @@ Sizes can be reduced with --requests / --max-prompt / --output-len / --model for
 
 ``--impl reference`` runs the reference implementation (ciresnave/lightbulb); it is a Rust
 crate that cannot be built on this image, so that arm prints an ``unavailable`` line.
+
+``--impl ref-algorithm`` (decode config) runs the reference's serving algorithm on this
+engine's kernels for comparison: one request at a time to completion (the job loop of
+``src/engine/model_runner.rs:383-398``), synchronous steps, NCCL-only tensor parallelism; it
+times the decode steps of ``--ref-requests`` requests on the device (max over ranks).
 """
 from __future__ import annotations
 
@@ -51,7 +56,9 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "ref-algorithm"])
+    ap.add_argument("--ref-requests", type=int, default=2,
+                    help="ref-algorithm arm: requests run one after another")
     ap.add_argument("--config", default="decode",
                     choices=["decode", "local-gen", "prefill-prefix", "spec", "awq-h2o"])
     ap.add_argument("--model", default=None, help="preset (default: the config's model)")
@@ -694,10 +701,70 @@ def bench_awq_h2o(args):
     return 0
 
 
+def bench_ref_algorithm(args):
+    """The reference's serving algorithm on this engine: requests run serially, batch 1."""
+    import torch
+    import torch.distributed as dist
+    from lightbulb_b200.config import (CacheConfig, EngineConfig, ParallelConfig,
+                                       SchedulerConfig, get_preset)
+    from lightbulb_b200.engine.llm_engine import LLMEngine
+    from lightbulb_b200.engine.sampling import SamplingParams
+    from lightbulb_b200.models.weights import random_packed_model
+    rank, world, local, dev, comm = _dist()
+    mcfg = get_preset(args.model)
+    steps = max(1, args.steps)
+    out_len = args.warmup + steps + 1
+    ecfg = EngineConfig(model=mcfg, cache=CacheConfig(block_size=args.block_size,
+                                                      gpu_memory_utilization=0.9),
+                        scheduler=SchedulerConfig(max_num_seqs=1, max_num_batched_tokens=2048,
+                                                  chunk_size=2048,
+                                                  max_model_len=args.max_prompt + out_len + 16),
+                        use_cuda_graphs=not args.no_graphs, overlap_decode=False,
+                        parallel=ParallelConfig(comm="nccl"))
+    packed = random_packed_model(mcfg, seed=args.seed, rank=rank, world=world, device=dev)
+    eng = LLMEngine(ecfg, packed, None, comm=comm, tp_rank=rank, tp_size=world)
+    prompts = _prompts(args, mcfg.vocab_size)[:max(1, args.ref_requests)]
+    sp = SamplingParams(temperature=0.0, max_tokens=out_len, ignore_eos=True, detokenize=False)
+    dev_ms, tokens = 0.0, 0
+    for i, p in enumerate(prompts):
+        s = eng.add_request(f"ref{i}", prompt_token_ids=p, params=sp)
+        _run_until_first_token(eng, [s])
+        for _ in range(args.warmup):
+            eng.step()
+        if comm is not None:
+            comm.barrier()
+        torch.cuda.synchronize()
+        eng.runner.enable_step_events()
+        for _ in range(steps):
+            tokens += len(eng.step())
+        dev_ms += eng.runner.step_events_total_ms()
+        eng.runner.disable_step_events()
+        while eng.has_unfinished():
+            eng.step()
+    if comm is not None:
+        dev_ms = comm.max_float(dev_ms)
+    value = tokens / (dev_ms / 1e3)
+    _emit(rank, {
+        "impl": "ref-algorithm",
+        "metric": "decode tok/s, p50 TTFT/ITL; Llama-3-8B shape, TP=1/2/4/8 B200, max over ranks",
+        "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_token": round(dev_ms / max(1, tokens), 4),
+        "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": {"model": describe(mcfg), "requests_timed": len(prompts),
+                   "parallelism": f"tp{world}", "comm": "nccl", "batch": 1,
+                   "cuda_graphs": not args.no_graphs},
+        "note": "reference serving algorithm (one request at a time, NCCL-only TP) on this "
+                "engine's kernels; not the reference build"})
+    _finish(eng, comm)
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return reference_arm(args)
+    if args.impl == "ref-algorithm":
+        return bench_ref_algorithm(args)
     return {"decode": bench_decode, "local-gen": bench_local_gen,
             "prefill-prefix": bench_prefill_prefix, "spec": bench_spec,
             "awq-h2o": bench_awq_h2o}[args.config](args)
