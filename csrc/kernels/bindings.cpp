@@ -30,6 +30,8 @@ void gemm_bf16_pair(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
                     const c10::optional<at::Tensor>& residual, int64_t mode, at::Tensor& err,
                     int64_t bt);
 void allreduce_prepare(int64_t base, int64_t max_elems, int64_t world);
+void gemv_bf16(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
+               const c10::optional<at::Tensor>& residual, int64_t mode);
 bool allreduce_rmsnorm_p2p(at::Tensor& h, const at::Tensor& inp, at::Tensor& x,
                            const at::Tensor& w, std::vector<int64_t> bases, int64_t rank,
                            int64_t max_elems, int64_t ctas, double eps, at::Tensor& err);
@@ -89,6 +91,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("trace_ptr") = 0, py::arg("ws") = py::none());
   m.def("allreduce_buffer_bytes", &lb::allreduce_buffer_bytes);
   m.def("allreduce_prepare", &lb::allreduce_prepare);
+  m.def("gemv_bf16", &lb::gemv_bf16, "weight-streaming GEMV for 1-4 tokens");
   m.def("allreduce_rmsnorm_p2p", &lb::allreduce_rmsnorm_p2p,
         "x += allreduce(partial); h = rmsnorm(x) * w, over NVLink peer memory");
   m.def("gemm_bf16_pair", &lb::gemm_bf16_pair, "bf16 GEMM on SM pairs (tcgen05 cta_group::2)",

@@ -23,6 +23,7 @@ else:
 
 EPI_STORE, EPI_SWIGLU, EPI_F32 = 0, 1, 2
 SPLITS_STREAMK = 1000   # gemm(splits=...): stream-K over (tile, k-block) in the persistent kernel
+GEMV_MAX_ROWS = 4       # gemm() with at most this many rows (and an automatic plan) uses the GEMV
 
 # Decode attention implementation: "tma" (warp-specialised TMA pipeline, default) or
 # "cpasync" (the generic paged kernel, also used for non-16 block sizes).
@@ -142,6 +143,11 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
             out = torch.empty(m, n, dtype=torch.bfloat16, device=a.device)
     if a.is_cuda:
         C = _need_c()
+        if 0 < m <= GEMV_MAX_ROWS and bt == 0 and splits == 0 and a.shape[1] % 8 == 0:
+            # 1-4 tokens: a pure weight stream, served by the GEMV kernel
+            C.gemv_bf16(a, w, out, residual, mode)
+            _launches[0] += 1
+            return out
         s = scratch(a.device)
         C.gemm_bf16(a, w, out, residual, mode, s.gemm_ws, s.gemm_counters, s.err, bt, splits,
                     None)

@@ -351,3 +351,41 @@ def test_gemm_streamk_epilogues():
     o32 = ops.gemm(a, w, mode=ops.EPI_F32, splits=ops.SPLITS_STREAMK)
     assert o32.dtype == torch.float32 and _rel(o32, full) < 5e-3
     ops.check_errors()
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 4])
+@pytest.mark.parametrize("n,k", [(4096, 4096), (1000, 2048), (257, 72), (6144, 14336)])
+def test_gemv_small_batch(m, n, k):
+    # 1-4 tokens go through the weight-streaming GEMV (odd N, K tails, long K)
+    torch.manual_seed(m * 31 + n)
+    a = torch.randn(m, k, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(n, k, device=DEV) * 0.05).to(torch.bfloat16)
+    ref = a.float() @ w.float().T
+    out = ops.gemm(a, w)
+    torch.cuda.synchronize()
+    assert out.shape == (m, n) and _rel(out, ref) < 1e-2
+    r = torch.randn(m, n, device=DEV).to(torch.bfloat16)
+    assert _rel(ops.gemm(a, w, residual=r), ref + r.float()) < 1e-2
+    o32 = ops.gemm(a, w, mode=ops.EPI_F32)
+    assert o32.dtype == torch.float32 and _rel(o32, ref) < 5e-3
+    # same result as the tensor-core path within bf16 rounding
+    tc = ops.gemm(a, w, bt=16)
+    assert _rel(out, tc.float()) < 1e-2
+    ops.check_errors()
+
+
+@pytest.mark.parametrize("m", [1, 4])
+def test_gemv_swiglu_and_lm_head(m):
+    from lightbulb_b200.models.weights import interleave_gate_up
+    f, k = 1536, 4096
+    a = torch.randn(m, k, device=DEV).to(torch.bfloat16)
+    g = (torch.randn(f, k, device=DEV) * 0.05).to(torch.bfloat16)
+    u = (torch.randn(f, k, device=DEV) * 0.05).to(torch.bfloat16)
+    w = interleave_gate_up(g, u)
+    ref = torch.nn.functional.silu(a.float() @ g.float().T) * (a.float() @ u.float().T)
+    out = ops.gemm(a, w, mode=ops.EPI_SWIGLU)
+    assert out.shape == (m, f) and _rel(out, ref) < 1e-2
+    head = (torch.randn(128256, k, device=DEV) * 0.02).to(torch.bfloat16)
+    lg = ops.gemm(a, head, mode=ops.EPI_F32)
+    assert _rel(lg, a.float() @ head.float().T) < 5e-3
+    ops.check_errors()
