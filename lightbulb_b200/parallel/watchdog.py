@@ -6,9 +6,9 @@ own monotonic clock, when each one last changed.  A peer whose counter has not m
 ``timeout_s`` is declared failed (no clock agreement between hosts is needed); a peer that
 has never beaten is only declared failed after ``startup_timeout_s`` (ranks start at different
 times); a store that stops answering (its host rank died) counts as a failure too.
-``on_failure`` is called once, from the monitor thread, with the set of failed ranks; :func:`attach` connects it to an
-:class:`~lightbulb_b200.engine.async_engine.AsyncEngine`, which then stops stepping, fails
-its in-flight requests and makes the server answer 503.
+``on_failure`` is called once, from the monitor thread, with the set of failed ranks;
+:func:`attach` connects it to an :class:`~lightbulb_b200.engine.async_engine.AsyncEngine`,
+which then stops stepping, fails its in-flight requests and makes the server answer 503.
 
 The reference has no multi-GPU failure handling.  This works entirely on the host: the
 device side of failure handling is the bounded waits of the collective kernels, which report
