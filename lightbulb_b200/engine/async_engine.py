@@ -81,16 +81,24 @@ class AsyncEngine:
         self._submit.put(("fail", reason))
 
     # ---- engine thread ----------------------------------------------------------------
+    def attach_control_plane(self, plane) -> None:
+        """Tensor-parallel serving: mirror every add / abort to the worker ranks (see
+        :mod:`lightbulb_b200.parallel.serving`) so that all ranks step in lockstep."""
+        self._plane = plane
+
     def _loop(self):
         eng = self.engine
         while not self._stop.is_set():
             drained = False
+            mirror = []
             while True:
                 try:
                     kind, payload = self._submit.get_nowait()
                 except queue.Empty:
                     break
                 drained = True
+                if kind in ("add", "abort"):
+                    mirror.append((kind, payload))
                 if kind == "add":
                     rid, kw = payload
                     try:
@@ -115,6 +123,14 @@ class AsyncEngine:
                         self._emit(rid, StreamItem(finished=True, finish_reason="error",
                                                    error=payload))
                         eng.abort(rid)
+            plane = getattr(self, "_plane", None)
+            if plane is not None:
+                if not self.healthy:
+                    plane.publish(None)            # workers stop: nobody steps again
+                    self._plane = None
+                elif mirror or eng.has_unfinished():
+                    # the workers apply the same submissions and step iff this rank steps
+                    plane.publish(mirror)
             if not self.healthy:
                 # failed: keep draining submissions (each fails at once), never step again
                 for rid in list(self._streams):
@@ -193,3 +209,7 @@ class AsyncEngine:
     def shutdown(self):
         self._stop.set()
         self._thread.join(timeout=10)
+        plane = getattr(self, "_plane", None)
+        if plane is not None:
+            plane.publish(None)
+            self._plane = None

@@ -134,7 +134,8 @@ class LLMEngine:
     def from_pretrained(cls, path: str, engine_cfg: Optional[EngineConfig] = None,
                         device: str = "cuda", **kw) -> "LLMEngine":
         from ..models.loader import load_model_dir
-        mcfg, packed, tok = load_model_dir(path, device=device)
+        mcfg, packed, tok = load_model_dir(path, device=device, tp_rank=kw.get("tp_rank", 0),
+                                           tp_size=kw.get("tp_size", 1))
         cfg = engine_cfg or EngineConfig()
         cfg.model = mcfg
         return cls(cfg, packed, tok, **kw)
@@ -145,7 +146,8 @@ class LLMEngine:
         from ..models.weights import random_packed_model
         cfg = engine_cfg or EngineConfig()
         cfg.model = mcfg
-        packed = random_packed_model(mcfg, seed=seed, device=device)
+        packed = random_packed_model(mcfg, seed=seed, rank=kw.get("tp_rank", 0),
+                                     world=kw.get("tp_size", 1), device=device)
         return cls(cfg, packed, None, **kw)
 
     # ---------------------------------------------------------------------------------
