@@ -64,6 +64,11 @@ class AsyncEngine:
         ``concurrent.futures.Future`` (``asyncio.wrap_future`` it from coroutines)."""
         import concurrent.futures
         fut = concurrent.futures.Future()
+        if getattr(self, "_plane", None) is not None:
+            # would run on rank 0 only: the ranks' engines would diverge (or see one KV shard)
+            fut.set_exception(NotImplementedError(
+                "engine-thread calls are not available under tensor-parallel serving"))
+            return fut
         self._submit.put(("call", (fn, fut)))
         return fut
 

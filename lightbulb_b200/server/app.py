@@ -403,8 +403,11 @@ def create_app(state: Optional[AppState] = None) -> FastAPI:
         if b.get("include_kv") and state.engine is not None:
             # requests + KV rows of their cached positions, written on the engine thread
             path = state.ckpt.kv_path(name)
-            info = await asyncio.wrap_future(state.engine.call(
-                lambda eng: save_engine_state(eng, path)))
+            try:
+                info = await asyncio.wrap_future(state.engine.call(
+                    lambda eng: save_engine_state(eng, path)))
+            except NotImplementedError as ex:
+                return _err(501, str(ex), "not_implemented")
             res = dict(res, kv=info)
         return res
 
@@ -425,6 +428,8 @@ def create_app(state: Optional[AppState] = None) -> FastAPI:
                     lambda eng: restore_engine_state(eng, path)))
             except ValueError as ex:
                 return _err(409, str(ex))
+            except NotImplementedError as ex:
+                return _err(501, str(ex), "not_implemented")
             out["resumed"] = ids
         return out
 

@@ -107,3 +107,19 @@ def test_state_routes_save_and_resume_with_kv(tmp_path):
         b.shutdown()
     assert r.status_code == 200 and r.json()["kv"]["kv_tensors"] == 1
     assert r2.status_code == 200 and r2.json()["resumed"] == ["keep"]
+
+
+def test_engine_calls_refused_under_tp_serving():
+    from lightbulb_b200.engine.async_engine import AsyncEngine
+    ae = AsyncEngine(_engine())
+
+    class Plane:                       # stands in for the control plane
+        def publish(self, msgs):
+            pass
+    ae.attach_control_plane(Plane())
+    try:
+        fut = ae.call(lambda eng: 1)
+        with pytest.raises(NotImplementedError):
+            fut.result(timeout=5)
+    finally:
+        ae.shutdown()
