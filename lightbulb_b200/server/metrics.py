@@ -1,8 +1,8 @@
 """Prometheus text exposition (``/metrics``) and the admin metrics snapshot.
 
 The reference's admin metrics return zeros (``src/api/admin.rs:184-194``); these come from
-the live engine: request/token counters, TTFT / ITL summaries, KV block usage, prefix-cache
-hit rate, speculative acceptance and step count.
+the live engine: request/token counters, TTFT / ITL quantiles and histograms, KV block usage,
+prefix-cache hit rate, speculative acceptance and step count.
 """
 from __future__ import annotations
 
@@ -16,6 +16,25 @@ def _q(vals: List[float], p: float) -> float:
         return 0.0
     s = sorted(vals)
     return s[min(len(s) - 1, int(p * len(s)))]
+
+
+TTFT_BUCKETS = (0.01, 0.025, 0.05, 0.1, 0.25, 0.5, 1.0, 2.5, 5.0, 10.0)
+ITL_BUCKETS = (0.001, 0.0025, 0.005, 0.01, 0.02, 0.05, 0.1, 0.25, 0.5)
+
+
+def _histogram(name: str, vals: List[float], bounds) -> List[str]:
+    """Prometheus histogram lines: cumulative bucket counts, sum and count."""
+    s = sorted(vals)
+    out = [f"# TYPE {name} histogram"]
+    i = 0
+    for b in bounds:
+        while i < len(s) and s[i] <= b:
+            i += 1
+        out.append(f'{name}_bucket{{le="{b}"}} {i}')
+    out.append(f'{name}_bucket{{le="+Inf"}} {len(s)}')
+    out.append(f"{name}_sum {sum(s)}")
+    out.append(f"{name}_count {len(s)}")
+    return out
 
 
 class Metrics:
@@ -61,4 +80,7 @@ class Metrics:
                   "spec_acceptance"):
             if k in s:
                 lines.append(f"lb_{k} {s[k]}")
+        if engine is not None:
+            lines += _histogram("lb_ttft_seconds", list(engine.stats.ttfts), TTFT_BUCKETS)
+            lines += _histogram("lb_itl_seconds", list(engine.stats.itls), ITL_BUCKETS)
         return "\n".join(lines) + "\n"

@@ -169,4 +169,15 @@ def test_extension_routes(tmp_path, engine):
             assert (await c.get("/v1/lightbulb/tools/list")).json()["tools"][0]["name"] == "calc"
             m = await c.get("/metrics")
             assert "lb_kv_blocks_total" in m.text
+            assert 'lb_ttft_seconds_bucket{le="+Inf"}' in m.text and "lb_itl_seconds_count" in m.text
     run(go())
+
+
+def test_metrics_histograms_are_cumulative():
+    from lightbulb_b200.server.metrics import ITL_BUCKETS, _histogram
+    lines = _histogram("lb_itl_seconds", [0.0005, 0.003, 0.003, 0.07, 2.0], ITL_BUCKETS)
+    assert lines[0] == "# TYPE lb_itl_seconds histogram"
+    buckets = [int(l.rsplit(" ", 1)[1]) for l in lines if "_bucket" in l]
+    assert buckets == sorted(buckets) and buckets[0] == 1 and buckets[-1] == 5
+    assert 'lb_itl_seconds_bucket{le="0.005"} 3' in lines
+    assert "lb_itl_seconds_count 5" in lines
