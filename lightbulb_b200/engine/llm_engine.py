@@ -15,6 +15,8 @@ sampled ids back device->host (``last_step_io``).
 """
 from __future__ import annotations
 
+import bisect
+import collections
 import logging
 import os
 import time
@@ -50,14 +52,37 @@ class RequestOutput:
     tool_call: Optional[dict] = None   # set when the request paused on a tool call
 
 
+TTFT_BUCKETS = (0.01, 0.025, 0.05, 0.1, 0.25, 0.5, 1.0, 2.5, 5.0, 10.0)     # seconds
+ITL_BUCKETS = (0.001, 0.0025, 0.005, 0.01, 0.02, 0.05, 0.1, 0.25, 0.5)
+
+
+class LatencySamples(collections.deque):
+    """Latency samples of a long-running engine: the newest ``window`` values (quantiles) plus
+    cumulative histogram counts, sum and count since start (monotone, as Prometheus expects),
+    so memory stays bounded however many tokens are served."""
+
+    def __init__(self, bounds, window: int = 200_000):
+        super().__init__(maxlen=window)
+        self.bounds = tuple(bounds)
+        self.bucket_counts = [0] * (len(self.bounds) + 1)     # last: above every bound
+        self.total = 0
+        self.sum = 0.0
+
+    def append(self, v: float) -> None:
+        super().append(v)
+        self.bucket_counts[bisect.bisect_left(self.bounds, v)] += 1
+        self.total += 1
+        self.sum += v
+
+
 @dataclass
 class EngineStats:
     steps: int = 0
     prompt_tokens: int = 0
     generated_tokens: int = 0
     preemptions: int = 0
-    ttfts: List[float] = field(default_factory=list)
-    itls: List[float] = field(default_factory=list)
+    ttfts: "LatencySamples" = field(default_factory=lambda: LatencySamples(TTFT_BUCKETS))
+    itls: "LatencySamples" = field(default_factory=lambda: LatencySamples(ITL_BUCKETS))
     finished: int = 0
 
 

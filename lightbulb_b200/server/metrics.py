@@ -18,8 +18,7 @@ def _q(vals: List[float], p: float) -> float:
     return s[min(len(s) - 1, int(p * len(s)))]
 
 
-TTFT_BUCKETS = (0.01, 0.025, 0.05, 0.1, 0.25, 0.5, 1.0, 2.5, 5.0, 10.0)
-ITL_BUCKETS = (0.001, 0.0025, 0.005, 0.01, 0.02, 0.05, 0.1, 0.25, 0.5)
+from ..engine.llm_engine import ITL_BUCKETS, TTFT_BUCKETS  # noqa: F401  (re-exported)
 
 
 def _histogram(name: str, vals: List[float], bounds) -> List[str]:
@@ -34,6 +33,19 @@ def _histogram(name: str, vals: List[float], bounds) -> List[str]:
     out.append(f'{name}_bucket{{le="+Inf"}} {len(s)}')
     out.append(f"{name}_sum {sum(s)}")
     out.append(f"{name}_count {len(s)}")
+    return out
+
+
+def _histogram_cumulative(name: str, st) -> List[str]:
+    """Histogram lines from cumulative counts kept since start (:class:`LatencySamples`)."""
+    out = [f"# TYPE {name} histogram"]
+    c = 0
+    for b, n in zip(st.bounds, st.bucket_counts):
+        c += n
+        out.append(f'{name}_bucket{{le="{b}"}} {c}')
+    out.append(f'{name}_bucket{{le="+Inf"}} {st.total}')
+    out.append(f"{name}_sum {st.sum}")
+    out.append(f"{name}_count {st.total}")
     return out
 
 
@@ -81,6 +93,9 @@ class Metrics:
             if k in s:
                 lines.append(f"lb_{k} {s[k]}")
         if engine is not None:
-            lines += _histogram("lb_ttft_seconds", list(engine.stats.ttfts), TTFT_BUCKETS)
-            lines += _histogram("lb_itl_seconds", list(engine.stats.itls), ITL_BUCKETS)
+            for name, st in (("lb_ttft_seconds", engine.stats.ttfts),
+                             ("lb_itl_seconds", engine.stats.itls)):
+                lines += _histogram_cumulative(name, st) if hasattr(st, "bucket_counts") \
+                    else _histogram(name, list(st), TTFT_BUCKETS if "ttft" in name
+                                    else ITL_BUCKETS)
         return "\n".join(lines) + "\n"

@@ -181,3 +181,16 @@ def test_metrics_histograms_are_cumulative():
     assert buckets == sorted(buckets) and buckets[0] == 1 and buckets[-1] == 5
     assert 'lb_itl_seconds_bucket{le="0.005"} 3' in lines
     assert "lb_itl_seconds_count 5" in lines
+
+
+def test_latency_samples_bounded_window_cumulative_counts():
+    from lightbulb_b200.engine.llm_engine import ITL_BUCKETS, LatencySamples
+    from lightbulb_b200.server.metrics import _histogram_cumulative
+    st = LatencySamples(ITL_BUCKETS, window=100)
+    for i in range(1000):
+        st.append(0.003 if i % 2 else 0.07)
+    assert len(st) == 100 and st.total == 1000          # memory bounded, counts are not
+    lines = _histogram_cumulative("lb_itl_seconds", st)
+    assert 'lb_itl_seconds_bucket{le="0.005"} 500' in lines
+    assert 'lb_itl_seconds_bucket{le="+Inf"} 1000' in lines
+    assert sorted(st)[0] == 0.003                         # quantiles over the window still work
