@@ -77,6 +77,8 @@ class AsyncEngine:
             self._emit(o.request_id, StreamItem(o.new_text, o.new_token_ids, o.finished,
                                                 o.finish_reason, o.prompt_tokens,
                                                 o.completion_tokens, o.cached_tokens))
+            if o.finished:
+                self.engine.release(o.request_id)     # keep the request table bounded
 
     def fail(self, reason: str) -> None:
         """Orderly stop after an external failure (e.g. a peer rank died): no further steps;
@@ -113,6 +115,7 @@ class AsyncEngine:
                                                    error=str(e)))
                 elif kind == "abort":
                     eng.abort(payload)
+                    eng.release(payload)
                     self._streams.pop(payload, None)
                 elif kind == "call":
                     fn, fut = payload

@@ -215,6 +215,18 @@ class LLMEngine:
     def abort(self, request_id: str) -> None:
         self.scheduler.abort(request_id)
 
+    def release(self, request_id: str) -> bool:
+        """Forget a finished request (its sequence and detokenizer state).  Long-running
+        front ends call this once a request's last output is delivered, so the request table
+        does not grow with every request served; returns False if it is unknown or still
+        running."""
+        s = self.seqs.get(request_id)
+        if s is None or not s.finished:
+            return False
+        del self.seqs[request_id]
+        self.detok.pop(request_id, None)
+        return True
+
     def has_unfinished(self) -> bool:
         return self._pending is not None or self.scheduler.has_work()
 

@@ -56,6 +56,9 @@ def run_worker(engine, plane: ControlPlane) -> int:
                     pass
             elif kind == "abort":
                 engine.abort(payload)
+                engine.release(payload)
         if engine.has_unfinished():
-            engine.step()
+            for o in engine.step():
+                if o.finished:
+                    engine.release(o.request_id)      # mirrors rank 0's bookkeeping
             steps += 1

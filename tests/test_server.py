@@ -194,3 +194,18 @@ def test_latency_samples_bounded_window_cumulative_counts():
     assert 'lb_itl_seconds_bucket{le="0.005"} 500' in lines
     assert 'lb_itl_seconds_bucket{le="+Inf"} 1000' in lines
     assert sorted(st)[0] == 0.003                         # quantiles over the window still work
+
+
+def test_async_engine_releases_finished_requests(engine):
+    from lightbulb_b200.engine.sampling import SamplingParams
+
+    async def go():
+        for i in range(3):
+            async for _ in engine.generate(prompt_token_ids=[5, 6, 7 + i],
+                                           params=SamplingParams(max_tokens=3,
+                                                                 ignore_eos=True)):
+                pass
+    run(go())
+    import time
+    time.sleep(0.2)
+    assert not [r for r, s in engine.engine.seqs.items() if s.finished]
