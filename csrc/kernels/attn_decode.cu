@@ -53,6 +53,7 @@ struct Args {
   float* part_o;
   float* part_lse;
   int total_rows;
+  int num_blocks;       // KV pool size: block ids outside [0, num_blocks) are reported
   int* err;
 };
 
@@ -157,9 +158,13 @@ __global__ void __launch_bounds__(THREADS, 2)
         uint8_t* sK = sKV + stage * STAGE_BYTES;
         uint8_t* sV = sK + TILE_BYTES;
         for (int b = 0; b < KT / BS; ++b) {
-          // A block id outside the pool gives a row coordinate outside the tensor map, which
-          // the TMA zero-fills: a corrupted table cannot read outside the KV pool here.
-          const int blk = btab[(kb >> 4) + (b < nblk ? b : 0)];
+          // A block id outside the pool (a corrupted table) is reported through the error
+          // word and replaced by block 0, so every TMA coordinate stays inside the tensor map.
+          int blk = btab[(kb >> 4) + (b < nblk ? b : 0)];
+          if (static_cast<unsigned>(blk) >= static_cast<unsigned>(a.num_blocks)) {
+            record_error(a.err, kErrBounds);
+            blk = 0;
+          }
           const int row = (blk * a.num_kv_heads + kvh) * BS;
           for (int h = 0; h < 2; ++h) {
             tma_load_2d(sK + h * HALF_BYTES + b * BS * 128, &tmK, &full[stage], h * 64, row, pol);
@@ -375,12 +380,15 @@ void paged_decode_tma(const at::Tensor& q, const at::Tensor& k_cache, const at::
   a.part_lse = nullptr;
   a.total_rows = q.size(0) * q.size(1);
   a.err = err.data_ptr<int>();
+  a.num_blocks = static_cast<int>(k_cache.size(0));
   if (a.num_splits > 1) {
     TORCH_CHECK(part_o.has_value() && part_lse.has_value(), "split-KV needs workspaces");
     a.part_o = part_o->data_ptr<float>();
     a.part_lse = part_lse->data_ptr<float>();
   }
   const uint64_t rows = static_cast<uint64_t>(k_cache.size(0)) * k_cache.size(1) * BS;
+  // Row coordinates are int32 (TMA) and computed in int from a checked block id.
+  TORCH_CHECK(rows < (1ull << 31), "decode_tma: KV pool too large for int32 row coordinates");
   const CUtensorMap tk = make_tmap_bf16_2d(k_cache.data_ptr(), D, rows, D * 2, 64, BS,
                                            CU_TENSOR_MAP_SWIZZLE_128B);
   const CUtensorMap tv = make_tmap_bf16_2d(v_cache.data_ptr(), D, rows, D * 2, 64, BS,
