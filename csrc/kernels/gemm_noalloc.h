@@ -45,6 +45,17 @@ enum {
 int lb_gemm_bf16_noalloc(const void* A, int lda, const void* W, int ldw, void* C, int ldc,
                          int M, int N, int K, int splits, cudaStream_t stream);
 
+// Kernel-side status of the most recent lb_gemm_bf16_noalloc call on the current device.
+// The GEMM kernel runs asynchronously, so a return of LB_NOALLOC_OK from the GEMM only means
+// the launch was accepted.  Its bounded waits (TMA arrivals, tensor-core commits, split-K
+// peers) record a nonzero code in the shared error word when they expire, in which case C is
+// incomplete.  This function waits for `stream` (pass the stream of the GEMM), then stores
+// that word in *kernel_error: 0 = the kernel finished normally; 1-7 = which wait expired
+// (1 TMA full, 2 shared-memory empty, 3 TMEM full, 4 TMEM empty, 5 split-K peer, 6 bounds,
+// 7 drain).  The word is cleared by the next GEMM call, so query it before issuing another.
+// Allocates nothing.  Returns LB_NOALLOC_OK or LB_NOALLOC_CUDA_ERROR / LB_NOALLOC_BAD_ARGS.
+int lb_gemm_bf16_noalloc_status(int* kernel_error, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

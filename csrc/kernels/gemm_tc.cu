@@ -1523,3 +1523,26 @@ extern "C" int lb_gemm_bf16_noalloc(const void* A, int lda, const void* W, int l
   if (e != cudaSuccess) return na_fail(LB_NOALLOC_CUDA_ERROR, "kernel launch", e);
   return LB_NOALLOC_OK;
 }
+
+extern "C" int lb_gemm_bf16_noalloc_status(int* kernel_error, cudaStream_t stream) {
+  if (!kernel_error) return na_fail(LB_NOALLOC_BAD_ARGS, "status: null kernel_error");
+  *kernel_error = 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return na_fail(LB_NOALLOC_CUDA_ERROR, "status: cudaGetDevice", e);
+  if (dev < 0 || dev >= kNaMaxDevices) return na_fail(LB_NOALLOC_BAD_ARGS, "device ordinal");
+  void* base = nullptr;
+  {
+    std::lock_guard<std::mutex> g(na_mu);
+    base = na_ptr[dev];
+  }
+  if (base == nullptr) return LB_NOALLOC_OK;  // no GEMM has run on this device yet
+  // The error word sits right after the tile counters; read it behind the caller's work on
+  // `stream` (a pageable destination makes the copy complete before cudaMemcpyAsync returns
+  // on some paths, so the stream is synchronised explicitly either way).
+  const int* err = reinterpret_cast<const int*>(base) + kNaCounterWords;
+  e = cudaMemcpyAsync(kernel_error, err, sizeof(int), cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return na_fail(LB_NOALLOC_CUDA_ERROR, "status: read error word", e);
+  return LB_NOALLOC_OK;
+}

@@ -5,6 +5,8 @@ callbacks, runtimes that own every allocation, real-time paths): its split-K scr
 a static device array inside the library.  This test allocates the inputs and outputs itself
 (the caller's job), calls the symbol twice in a row through ctypes and compares each result
 with the regular entry point (``ops.gemm`` with the same split count) and an fp32 reference.
+After each call it reads the kernel's error word through ``lb_gemm_bf16_noalloc_status``,
+the non-allocating way such a caller learns that a bounded wait inside the kernel expired.
 It runs last so that a failure here never hides the other tests' results.
 """
 import ctypes
@@ -26,6 +28,16 @@ def _lib():
     return fn
 
 
+def _status(stream):
+    from lightbulb_b200 import _C
+    fn = ctypes.CDLL(_C.__file__).lb_gemm_bf16_noalloc_status
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.POINTER(ctypes.c_int), ctypes.c_void_p]
+    code = ctypes.c_int(-1)
+    rc = fn(ctypes.byref(code), stream)
+    return rc, code.value
+
+
 def _rel(a, b):
     return ((a.float() - b.float()).norm() / (b.float().norm() + 1e-12)).item()
 
@@ -45,6 +57,7 @@ def test_noalloc_matches_regular_entry_point(m, n, k, splits):
         out = torch.full((m, n), float("nan"), device="cuda", dtype=torch.bfloat16)
         rc = fn(a.data_ptr(), k, w.data_ptr(), k, out.data_ptr(), n, m, n, k, splits, stream)
         assert rc == 0
+        assert _status(stream) == (0, 0)      # no bounded wait expired inside the kernel
         torch.cuda.synchronize()
         assert _rel(out, regular) < 1e-2
         assert _rel(out, ref) < 1e-2
