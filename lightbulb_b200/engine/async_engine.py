@@ -131,6 +131,7 @@ class AsyncEngine:
                         self._emit(rid, StreamItem(finished=True, finish_reason="error",
                                                    error=payload))
                         eng.abort(rid)
+                        eng.release(rid)
             plane = getattr(self, "_plane", None)
             if plane is not None:
                 if not self.healthy:
@@ -145,6 +146,7 @@ class AsyncEngine:
                     self._emit(rid, StreamItem(finished=True, finish_reason="error",
                                                error=self.last_error))
                     eng.abort(rid)
+                    eng.release(rid)
                 if not drained:
                     time.sleep(self._idle)
                 continue

@@ -17,6 +17,7 @@ from __future__ import annotations
 
 import bisect
 import collections
+import threading
 import logging
 import os
 import time
@@ -59,20 +60,28 @@ ITL_BUCKETS = (0.001, 0.0025, 0.005, 0.01, 0.02, 0.05, 0.1, 0.25, 0.5)
 class LatencySamples(collections.deque):
     """Latency samples of a long-running engine: the newest ``window`` values (quantiles) plus
     cumulative histogram counts, sum and count since start (monotone, as Prometheus expects),
-    so memory stays bounded however many tokens are served."""
+    so memory stays bounded however many tokens are served.  The engine thread appends while
+    server handlers read: :meth:`snapshot` copies under the same lock as :meth:`append`, and
+    the window is small enough (8192) that sorting a copy costs well under a millisecond."""
 
-    def __init__(self, bounds, window: int = 200_000):
+    def __init__(self, bounds, window: int = 8192):
         super().__init__(maxlen=window)
         self.bounds = tuple(bounds)
         self.bucket_counts = [0] * (len(self.bounds) + 1)     # last: above every bound
         self.total = 0
         self.sum = 0.0
+        self._lock = threading.Lock()
 
     def append(self, v: float) -> None:
-        super().append(v)
-        self.bucket_counts[bisect.bisect_left(self.bounds, v)] += 1
-        self.total += 1
-        self.sum += v
+        with self._lock:
+            super().append(v)
+            self.bucket_counts[bisect.bisect_left(self.bounds, v)] += 1
+            self.total += 1
+            self.sum += v
+
+    def snapshot(self) -> list:
+        with self._lock:
+            return list(self)
 
 
 @dataclass

@@ -11,7 +11,9 @@ import threading
 from typing import Dict, List
 
 
-def _q(vals: List[float], p: float) -> float:
+def _q(vals, p: float) -> float:
+    if hasattr(vals, "snapshot"):
+        vals = vals.snapshot()            # a consistent copy taken under the writer's lock
     if not vals:
         return 0.0
     s = sorted(vals)
