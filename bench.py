@@ -258,9 +258,14 @@ def bench_decode(args):
         pass
     clocks = ClockSampler(uuid)
     clocks.start()
+    eng.runner.enable_step_events()
+    gen_tokens = 0
+    gen_w0 = time.perf_counter()
     for _ in range(args.warmup):
-        eng.step()
+        gen_tokens += len(eng.step())
     ops.check_errors(dev)
+    gen_dev_ms = eng.runner.step_events_total_ms()
+    eng.runner.disable_step_events()
     n_active = sum(1 for s in seqs if not s.finished)
 
     # ---- phase 3: timed decode steps ----
@@ -285,11 +290,24 @@ def bench_decode(args):
     eng.runner.disable_step_events()
     clk = clocks.stop()
     ops.check_errors(dev)
+    # ---- phase 4 (not part of the timed K steps): the rest of the generation, so the line
+    # also carries decode throughput over every output token, not only the early window ----
+    gen_tokens += tokens
+    gen_dev_ms += dev_ms
+    eng.runner.enable_step_events()
+    while eng.has_unfinished():
+        gen_tokens += len(eng.step())
+    gen_dev_ms += eng.runner.step_events_total_ms()
+    gen_wall = time.perf_counter() - gen_w0
+    eng.runner.disable_step_events()
+    ops.check_errors(dev)
     if comm is not None:
         comm.barrier()
         dev_ms = comm.max_float(dev_ms)
         wall = comm.max_float(wall)
-    itls = sorted(eng.stats.itls) if eng.stats.itls else [0.0]
+        gen_dev_ms = comm.max_float(gen_dev_ms)
+        gen_wall = comm.max_float(gen_wall)
+    itls = sorted(x for s in seqs for x in s.itls()) or [0.0]
 
     value = tokens / (dev_ms / 1e3)
     e2e = tokens / wall
@@ -312,6 +330,11 @@ def bench_decode(args):
             "itl_p50_ms": round(1e3 * itls[len(itls) // 2], 3),
             "prefill_phase_s": round(prefill_s, 3),
             "active_seqs": n_active,
+            "whole_generation": {"decode_tok_s": round(gen_tokens / (gen_dev_ms / 1e3), 2),
+                                 "e2e_tok_s": round(gen_tokens / gen_wall, 2),
+                                 "tokens": gen_tokens, "device_ms": round(gen_dev_ms, 2),
+                                 "note": "every decode step after the last first token, "
+                                         "warm-up and timed steps included"},
             "e2e": {"value": round(e2e, 2), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d // max(1, args.steps),
                     "d2h_bytes_per_step": d2h // max(1, args.steps),
