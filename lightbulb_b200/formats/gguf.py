@@ -194,6 +194,8 @@ LAYER_MAP = {
     "mlp.gate_proj.weight": "ffn_gate.weight",
     "mlp.up_proj.weight": "ffn_up.weight",
     "mlp.down_proj.weight": "ffn_down.weight",
+    "self_attn.q_norm.weight": "attn_q_norm.weight",     # Qwen3
+    "self_attn.k_norm.weight": "attn_k_norm.weight",
 }
 
 
@@ -231,6 +233,7 @@ def config_from_gguf(md: dict) -> ModelConfig:
     p = f"{arch}."
     hs = int(_meta(md, p + "embedding_length", p + "n_embd"))
     nh = int(_meta(md, p + "attention.head_count", p + "n_head"))
+    head_dim = int(_meta(md, p + "attention.key_length", default=0) or 0)
     toks = md.get("tokenizer.ggml.tokens")
     vocab = int(_meta(md, p + "vocab_size", default=len(toks) if toks else 32000))
     return ModelConfig(
@@ -243,7 +246,7 @@ def config_from_gguf(md: dict) -> ModelConfig:
         max_position_embeddings=int(_meta(md, p + "context_length", default=4096)),
         bos_token_id=int(md.get("tokenizer.ggml.bos_token_id", 1)),
         eos_token_id=int(md.get("tokenizer.ggml.eos_token_id", 2)),
-        tie_word_embeddings=False)
+        tie_word_embeddings=False, head_dim=head_dim, qk_norm=arch == "qwen3")
 
 
 def save_llama_gguf(path: str, cfg: ModelConfig, weights: Dict[str, torch.Tensor],

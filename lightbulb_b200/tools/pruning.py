@@ -95,6 +95,25 @@ def prune(cfg, w: Dict[str, torch.Tensor], method: str = "wanda", sparsity: floa
     return out, man
 
 
+def map_manifest(man: PruneManifest, tensor_names) -> Dict[str, str]:
+    """Manifest entries (HF layer names) -> the names the target checkpoint uses, whatever its
+    family (GGUF llama.cpp names, GPT ``h.N`` names or HF names; detected from
+    ``tensor_names``, reference ``src/pruning/name_mapping.rs:100-128``).  Entries with no
+    counterpart in the checkpoint are left out."""
+    from ..formats.name_map import MISTRAL, TensorNameMapper, translate
+    names = list(tensor_names)
+    dst = TensorNameMapper(names)
+    src = TensorNameMapper([e.name for e in man.entries], MISTRAL)
+    present = set(names)
+    out = {}
+    for e in man.entries:
+        arch = dst.architecture if dst.architecture in ("llama", "gpt", "mistral") else "llama"
+        t = translate(e.name, src, arch)
+        if t is not None and t in present:
+            out[e.name] = t
+    return out
+
+
 def apply_to_gguf(raw: np.ndarray, ggml_type: int, n: int, k: int, mask: torch.Tensor) -> bytes:
     """Dequantise a GGUF tensor, zero the masked weights and requantise to the same type."""
     from .. import _native as N
