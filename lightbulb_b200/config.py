@@ -33,6 +33,9 @@ class ModelConfig:
     tie_word_embeddings: bool = False
     bos_token_id: int = 1
     eos_token_id: int | list[int] = 2
+    # Qwen3: per-head RMSNorm of q and k (weights of width head_dim) before RoPE
+    # (reference src/model/awq_qwen3.rs:188-189,259-267)
+    qk_norm: bool = False
 
     def __post_init__(self) -> None:
         if self.head_dim == 0:
@@ -73,8 +76,8 @@ class ModelConfig:
     # ---- HF config.json interop -------------------------------------------------------
     def to_hf_dict(self) -> dict:
         return {
-            "architectures": ["LlamaForCausalLM"],
-            "model_type": "llama",
+            "architectures": ["Qwen3ForCausalLM" if self.qk_norm else "LlamaForCausalLM"],
+            "model_type": "qwen3" if self.qk_norm else "llama",
             "vocab_size": self.vocab_size,
             "hidden_size": self.hidden_size,
             "intermediate_size": self.intermediate_size,
@@ -96,7 +99,9 @@ class ModelConfig:
     def from_hf_dict(cls, d: dict) -> "ModelConfig":
         nh = int(d["num_attention_heads"])
         hs = int(d["hidden_size"])
+        arch = " ".join(d.get("architectures") or []) + " " + str(d.get("model_type", ""))
         return cls(
+            qk_norm="qwen3" in arch.lower(),
             name=d.get("lb200_name", d.get("model_type", "llama")),
             vocab_size=int(d["vocab_size"]),
             hidden_size=hs,
@@ -153,7 +158,17 @@ PRESETS: dict[str, ModelConfig] = {
                         intermediate_size=11008, num_layers=32, num_heads=32, num_kv_heads=32),
     "llama2-7b": _preset(name="llama2-7b", vocab_size=32000, hidden_size=4096,
                          intermediate_size=11008, num_layers=32, num_heads=32, num_kv_heads=32),
+    # Qwen3-8B shape (per-head q/k RMSNorm); the reference's AwqQwen3 architecture.
+    "qwen3-8b": _preset(name="qwen3-8b", vocab_size=151936, hidden_size=4096,
+                        intermediate_size=12288, num_layers=36, num_heads=32, num_kv_heads=8,
+                        head_dim=128, rope_theta=1e6, rms_norm_eps=1e-6,
+                        max_position_embeddings=40960, bos_token_id=151643,
+                        eos_token_id=[151645, 151643], qk_norm=True),
     # Small shapes for tests.
+    "qwen3-tiny-test": _preset(name="qwen3-tiny-test", vocab_size=512, hidden_size=512,
+                               intermediate_size=1024, num_layers=2, num_heads=4,
+                               num_kv_heads=2, head_dim=128, rope_theta=1e6, rms_norm_eps=1e-6,
+                               max_position_embeddings=4096, qk_norm=True),
     "tiny-test": _preset(name="tiny-test", vocab_size=512, hidden_size=256,
                          intermediate_size=512, num_layers=2, num_heads=8, num_kv_heads=2,
                          rope_theta=1e4, max_position_embeddings=4096),
@@ -202,9 +217,12 @@ class ParallelConfig:
     tensor_parallel_size: int = 1
     pipeline_parallel_size: int = 1
     # Row-parallel partial sums under tensor parallelism:
-    #   "p2p"   one-launch push all-reduce over NVLink peer memory (parallel/allreduce.py);
-    #   "fused" GEMM scatter epilogue + reduce/RMSNorm/all-gather kernel (parallel/fused.py);
-    #   "nccl"  NCCL all_reduce only.
+    #   "p2p"       row-parallel exchange over NVLink peer memory: the GEMM epilogue pushes rows
+    #               to their owners, one kernel reduces + adds the residual + RMSNorm + gathers
+    #               (parallel/rowpar.py);
+    #   "allreduce" one-launch push all-reduce, then a separate add + RMSNorm (allreduce.py);
+    #   "fused"     flag-signalled GEMM scatter + reduce/RMSNorm/all-gather (parallel/fused.py);
+    #   "nccl"      NCCL all_reduce only.
     comm: str = "p2p"
 
 

@@ -145,7 +145,9 @@ def load_model_dir(path: str, device="cuda", tp_rank: int = 0, tp_size: int = 1,
         for i in range(cfg.num_layers):
             lw = dict(qlayers)
             p = f"model.layers.{i}."
-            for nm in ("input_layernorm.weight", "post_attention_layernorm.weight"):
-                lw[p + nm] = w[p + nm]
+            for nm in ("input_layernorm.weight", "post_attention_layernorm.weight",
+                       "self_attn.q_norm.weight", "self_attn.k_norm.weight"):
+                if p + nm in w:
+                    lw[p + nm] = w[p + nm]
             packed["layers"][i] = pack_layer_quant(cfg, lw, i, tp_rank, tp_size, device)
     return cfg, packed, tok

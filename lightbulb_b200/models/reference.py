@@ -3,7 +3,8 @@
 This restates the math of the reference's candle Llama path in plain PyTorch fp32:
 RMSNorm ``x * rsqrt(mean(x^2) + eps) * g`` (``src/model/fused_rmsnorm.rs:47-110``),
 rotate-half RoPE over the full head dim (``src/model/custom_attention.rs:687-728``),
-GQA attention with causal mask (``custom_attention.rs:741-858``), SwiGLU MLP
+GQA attention with causal mask (``custom_attention.rs:741-858``), Qwen3's per-head q/k RMSNorm
+(``src/model/awq_qwen3.rs:259-267``), SwiGLU MLP
 (``src/model/mlp_wrapper.rs:154-199``) and greedy argmax with first-max tie-break
 (``src/model_fuel/generate.rs:54-65``).  It is deliberately unoptimised and independent of
 every CUDA kernel in this package so that kernel tests compare against it.
@@ -102,6 +103,9 @@ class ReferenceLlama:
             q = (h @ w[p + "self_attn.q_proj.weight"].T).view(t, c.num_heads, c.head_dim)
             k = (h @ w[p + "self_attn.k_proj.weight"].T).view(t, c.num_kv_heads, c.head_dim)
             v = (h @ w[p + "self_attn.v_proj.weight"].T).view(t, c.num_kv_heads, c.head_dim)
+            if c.qk_norm:   # Qwen3 (src/model/awq_qwen3.rs:259-267): per-head norm, then RoPE
+                q = rms_norm(q, w[p + "self_attn.q_norm.weight"], c.rms_norm_eps)
+                k = rms_norm(k, w[p + "self_attn.k_norm.weight"], c.rms_norm_eps)
             q = apply_rope(q, cos, sin)
             k = apply_rope(k, cos, sin)
             self.k_cache[i] = torch.cat([self.k_cache[i], k], 0)

@@ -48,7 +48,28 @@ def weight_shapes(cfg: ModelConfig) -> Dict[str, tuple]:
         shapes[p + "mlp.gate_proj.weight"] = (f, h)
         shapes[p + "mlp.up_proj.weight"] = (f, h)
         shapes[p + "mlp.down_proj.weight"] = (h, f)
+        if cfg.qk_norm:
+            shapes[p + "self_attn.q_norm.weight"] = (cfg.head_dim,)
+            shapes[p + "self_attn.k_norm.weight"] = (cfg.head_dim,)
     return shapes
+
+
+def pad_norm(w: torch.Tensor, d: int, dp: int) -> torch.Tensor:
+    """Per-head norm weight [d] -> [dp] (padded lanes of q / k are zero, so their weight is
+    irrelevant; zero keeps them zero)."""
+    if dp == d:
+        return w
+    out = torch.zeros(dp, dtype=w.dtype, device=w.device)
+    out[:d] = w
+    return out
+
+
+def qk_norm_weights(cfg: ModelConfig, w, p: str, dev) -> Dict[str, torch.Tensor]:
+    if not cfg.qk_norm:
+        return {}
+    dp = cfg.head_dim_padded
+    return {"q_norm": dev(pad_norm(w[p + "self_attn.q_norm.weight"], cfg.head_dim, dp)),
+            "k_norm": dev(pad_norm(w[p + "self_attn.k_norm.weight"], cfg.head_dim, dp))}
 
 
 def random_tensor(name: str, shape: tuple, seed: int, dtype: torch.dtype, device="cpu",
@@ -197,6 +218,7 @@ def pack_layer(cfg: ModelConfig, w: Dict[str, torch.Tensor], i: int, rank: int =
         "o": dev(ow),
         "gate_up": dev(interleave_gate_up(gw, uw)),
         "down": dev(dw),
+        **qk_norm_weights(cfg, w, p, dev),
     }
 
 
@@ -275,7 +297,9 @@ def pack_layer_quant(cfg: ModelConfig, lw: Dict[str, object], i: int, rank: int 
         ow = pad_head_cols(ow.to(device).dequantize(torch.bfloat16), hq, d, dp)
     return {"ln_in": nrm("input_layernorm.weight"), "ln_post": nrm("post_attention_layernorm.weight"),
             "qkv": dev(cat_rows([qw, kw, vw])), "o": dev(ow),
-            "gate_up": dev(interleave_rows(gw, uw)), "down": dev(dw)}
+            "gate_up": dev(interleave_rows(gw, uw)), "down": dev(dw),
+            **qk_norm_weights(cfg, lw, p,
+                              lambda t: t.to(device=device, dtype=torch.bfloat16).contiguous())}
 
 
 def random_packed_awq_model(cfg: ModelConfig, seed: int = 0, rank: int = 0, world: int = 1,
@@ -301,8 +325,11 @@ def random_packed_awq_model(cfg: ModelConfig, seed: int = 0, rank: int = 0, worl
                      "self_attn.o_proj", "mlp.gate_proj", "mlp.up_proj", "mlp.down_proj"):
             n_, k_ = shapes[p + name + ".weight"]
             lw[p + name + ".weight"] = qlin(n_, k_)
-        for name in ("input_layernorm.weight", "post_attention_layernorm.weight"):
-            lw[p + name] = random_tensor(p + name, shapes[p + name], seed, torch.bfloat16, device)
+        for name in ("input_layernorm.weight", "post_attention_layernorm.weight",
+                     "self_attn.q_norm.weight", "self_attn.k_norm.weight"):
+            if p + name in shapes:
+                lw[p + name] = random_tensor(p + name, shapes[p + name], seed, torch.bfloat16,
+                                             device)
         layers.append(pack_layer_quant(cfg, lw, i, rank, world, device))
     top = {n: random_tensor(n, shapes[n], seed, torch.bfloat16, device)
            for n in ("model.embed_tokens.weight", "model.norm.weight", "lm_head.weight")

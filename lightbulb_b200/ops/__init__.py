@@ -263,13 +263,16 @@ def rope_table(max_pos: int, head_dim: int, theta: float, device) -> torch.Tenso
 
 def rope_kv(qkv: torch.Tensor, positions: torch.Tensor, slots: Optional[torch.Tensor],
             cos_sin: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, hq: int,
-            hkv: int) -> None:
+            hkv: int, q_norm: Optional[torch.Tensor] = None,
+            k_norm: Optional[torch.Tensor] = None, norm_dim: int = 0,
+            eps: float = 1e-6) -> None:
     """Rotate q (in place) and k of ``qkv`` [T, (hq + 2 hkv) D] and write k, v to their slots.
     D = the cache's head width; the rotation covers the first ``cos_sin.shape[1]`` lanes of
-    each head (the true head_dim when heads are zero-padded)."""
+    each head (the true head_dim when heads are zero-padded).  ``q_norm`` / ``k_norm`` [D]:
+    per-head RMSNorm (over ``norm_dim`` lanes) of q / k before the rotation (Qwen3)."""
     if qkv.is_cuda:
         _need_c().rope_kv(qkv, positions, slots, cos_sin, k_cache, v_cache, hq, hkv,
-                          scratch(qkv.device).err)
+                          scratch(qkv.device).err, q_norm, k_norm, norm_dim, eps)
         _launches[0] += 1
         return
     d = k_cache.shape[-1]           # head stride (padded width)
@@ -279,6 +282,12 @@ def rope_kv(qkv: torch.Tensor, positions: torch.Tensor, slots: Optional[torch.Te
     cs = cos_sin[positions.long()]
     c, s = cs[:, None, :half], cs[:, None, half:]
     x = qkv[:, :(hq + hkv) * d].view(t, hq + hkv, d).float()
+    nd = norm_dim or r
+    for lo, hi, nw in ((0, hq, q_norm), (hq, hq + hkv, k_norm)):
+        if nw is not None:
+            xs = x[:, lo:hi]
+            inv = torch.rsqrt(xs.pow(2).sum(-1, keepdim=True) / nd + eps)
+            x[:, lo:hi] = (xs * inv * nw.float()).to(qkv.dtype).float()
     x1, x2 = x[..., :half], x[..., half:r]
     rot = torch.cat([x1 * c - x2 * s, x1 * s + x2 * c, x[..., r:]], -1).to(qkv.dtype)
     qkv[:, :hq * d].copy_(rot[:, :hq].reshape(t, -1))

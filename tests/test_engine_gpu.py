@@ -86,6 +86,31 @@ def test_engine_padded_heads_gpu(hidden, heads, kv):
             assert int(torch.argmax(lg[i])) == t or (top2[0] - top2[1]) < 0.05
 
 
+def test_qwen3_engine_gpu():
+    # Qwen3 (per-head q/k RMSNorm fused into the RoPE + KV kernel) on the GPU engine with CUDA
+    # graphs, against the fp32 oracle
+    cfg = get_preset("qwen3-tiny-test", vocab_size=1024)
+    w = random_weights(cfg, seed=6, std=0.05)
+    w = {k: v.to(torch.bfloat16).float() for k, v in w.items()}
+    packed = pack_model(cfg, w, dtype=torch.bfloat16, device="cuda")
+    ecfg = EngineConfig(model=cfg, cache=CacheConfig(num_blocks=64, block_size=16),
+                        scheduler=SchedulerConfig(max_num_seqs=4, max_num_batched_tokens=96,
+                                                  chunk_size=48, max_model_len=512),
+                        use_cuda_graphs=True)
+    eng = LLMEngine(ecfg, packed)
+    ref = ReferenceLlama(cfg, w)
+    prompts = [list(range(3, 60)), [11, 12, 13]]
+    sp = SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True)
+    seqs = eng.generate(prompt_token_ids=prompts, params=sp)
+    ops.check_errors()
+    for p, s in zip(prompts, seqs):
+        ref.reset()
+        lg = ref.forward(torch.tensor(p + s.output_token_ids[:-1]))[len(p) - 1:]
+        for i, t in enumerate(s.output_token_ids):
+            top2 = torch.topk(lg[i], 2).values
+            assert int(torch.argmax(lg[i])) == t or (top2[0] - top2[1]) < 0.05
+
+
 def test_overlapped_decode_matches_sync_gpu():
     # CUDA-graph decode with overlap (next step launched before the previous ids are read
     # back; pinned inputs double-buffered) must emit the synchronous engine's tokens

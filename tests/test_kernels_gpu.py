@@ -115,6 +115,44 @@ def test_rope_kv():
     assert torch.equal(vc.cpu(), vc2)
 
 
+@pytest.mark.parametrize("rot", [64, 96, 128])
+@pytest.mark.parametrize("qk_norm", [False, True])
+def test_rope_kv_warp_widths_and_qk_norm(rot, qk_norm):
+    # warp-per-head kernel: rotary widths of zero-padded heads (64, 96) and full 128, with and
+    # without Qwen3's per-head q/k RMSNorm, against the CPU restatement (fp32 oracle math)
+    hq, hkv, d, bs = 8, 2, 128, 16
+    T = 37
+    g = torch.Generator().manual_seed(rot + qk_norm)
+    qkv = torch.randn(T, (hq + 2 * hkv) * d, generator=g).to(torch.bfloat16)
+    v3 = qkv.view(T, hq + 2 * hkv, d)
+    v3[:, :, rot:] = 0                      # padded lanes are zero in the model layout
+    pos = torch.randint(0, 900, (T,), generator=g, dtype=torch.int32)
+    slots = torch.randperm(64 * bs, generator=g)[:T].to(torch.int32)
+    slots[5] = -1
+    cs = ops.rope_table(1024, rot, 1e6, torch.device("cpu"))
+    qn = kn = None
+    if qk_norm:
+        qn = torch.zeros(d, dtype=torch.bfloat16)
+        kn = torch.zeros(d, dtype=torch.bfloat16)
+        qn[:rot] = (1 + 0.2 * torch.randn(rot, generator=g)).to(torch.bfloat16)
+        kn[:rot] = (1 + 0.2 * torch.randn(rot, generator=g)).to(torch.bfloat16)
+    kc = torch.zeros(64, hkv, bs, d, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    qg, kg, vg = qkv.to(DEV), kc.to(DEV), vc.to(DEV)
+    ops.scratch(torch.device(DEV)).err.zero_()
+    ops.rope_kv(qg, pos.to(DEV), slots.to(DEV), cs.to(DEV), kg, vg, hq, hkv,
+                q_norm=None if qn is None else qn.to(DEV),
+                k_norm=None if kn is None else kn.to(DEV), norm_dim=rot, eps=1e-6)
+    torch.cuda.synchronize()
+    ops.check_errors(torch.device(DEV))
+    qc = qkv.clone()
+    ops.rope_kv(qc, pos, slots, cs, kc, vc, hq, hkv, q_norm=qn, k_norm=kn, norm_dim=rot,
+                eps=1e-6)
+    assert _rel(qg[:, :hq * d].cpu(), qc[:, :hq * d]) < 1e-2
+    assert _rel(kg.cpu(), kc) < 1e-2
+    assert torch.equal(vg.cpu(), vc)
+
+
 def _paged_setup(seq_lens, q_lens, hq, hkv, d=128, bs=16, seed=0):
     g = torch.Generator().manual_seed(seed)
     nb_per = [(L + bs - 1) // bs for L in seq_lens]
