@@ -74,7 +74,7 @@ def parse():
     ap.add_argument("--h2o-sinks", type=int, default=4)
     ap.add_argument("--block-size", type=int, default=16)
     ap.add_argument("--max-batched-tokens", type=int, default=16384)
-    ap.add_argument("--comm", default="p2p", choices=["nccl", "fused", "p2p"],
+    ap.add_argument("--comm", default="p2p", choices=["nccl", "fused", "p2p", "allreduce"],
                     help="TP partial-sum collective (engine option parallel.comm)")
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--seed", type=int, default=1234)

@@ -3,7 +3,7 @@
 // The reference's TP "all-reduce" (src/multi_gpu/tensor_parallel.rs:119-133) copies each
 // partial to device 0 and adds them serially.  This kernel replaces NCCL's ring all-reduce for
 // the small (0.1-4 MB) partial sums of a decode step, where latency, not bandwidth, dominates.
-// It uses no flags, fences or handshakes: the data is its own flag.
+// It uses no flags or handshakes: the data is its own flag.
 //
 //   receive buffers of every rank (CUDA IPC, opened by every peer), initialised to the
 //   sentinel 0xFFFF in every bf16 lane (a NaN that is never sent: outgoing 0xFFFF lanes are
@@ -19,11 +19,17 @@
 //     AG     rank r polls recv2[par] for every other slice, copies it out, writes the sentinel.
 //
 // Reuse: a receive slot of parity p is written again in epoch e + 2; a peer can reach that
-// epoch only after this rank finished epoch e + 1 (it needs this rank's pushes of e + 2, issued
-// by a later kernel), so the sentinel written back in epoch e is in place.  Partial visibility
-// of a 16-byte store is harmless: every lane is checked.  Every poll is bounded in time: on
-// expiry the kernel records an error code and stops.  Peer memory is written with plain stores
-// only; the only loads are of this GPU's own memory.
+// epoch only after finishing epoch e + 1, which needs this rank's pushes of e + 1, issued by a
+// later launch than this rank's sentinel write-backs of epoch e: the write-back is performed at
+// this GPU's L2 (the point of coherence of its memory) before the later launch starts, and the
+// peer's next store reaches that L2 only after the peer observed a push issued by the later
+// launch, so the peer's store follows the write-back in coherence order (the full argument is
+// in tp_rowpar.cu, which uses the same slots discipline).  An explicit release fence at launch
+// start (comm_fence_mode 1 or 2) is available; measured at TP2 on 2 MiB it costs ~7 us (every
+// thread) or ~4 us (one per CTA) of an 8 us all-reduce.  Partial visibility of a 16-byte store is harmless:
+// every lane is checked.  Every poll is bounded in time: on expiry the kernel records an error
+// code and stops.  Peer memory is written with plain stores only; the only loads are of this
+// GPU's own memory.
 #include <ATen/cuda/CUDAContext.h>
 #include <functional>
 #include <torch/extension.h>
@@ -49,6 +55,7 @@ struct Args {
   int64_t max_per;                // slice capacity (vectors) of one recv1 source
   int64_t max_vec;                // capacity (vectors) of one recv2 parity
   int world, rank;
+  int fence_mode;                 // 1: every thread fences at launch start; 2: thread 0 only
   int* err;
 };
 
@@ -77,6 +84,10 @@ __device__ __forceinline__ uint4 canon4(uint4 v) {
   return make_uint4(canon(v.x), canon(v.y), canon(v.z), canon(v.w));
 }
 
+__device__ __forceinline__ void fence_acq_rel_sys() {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
 // Poll a local slot until every lane is written; false when the kernel's time budget ran out.
 __device__ __forceinline__ bool poll(const uint4* p, uint4& v, uint64_t t0) {
   uint32_t it = 0;
@@ -97,9 +108,18 @@ __device__ __forceinline__ void add8(float (&acc)[8], const uint4& v) {
   }
 }
 
+// Launch-start ordering (see the file comment): mode 1 = fence.acq_rel.sys in every thread,
+// mode 2 = in thread 0 before the CTA barrier that precedes every store, 0 = none (measurement).
+__device__ __forceinline__ void start_fence(int mode) {
+  if (mode == 1 || (mode == 2 && threadIdx.x == 0)) fence_acq_rel_sys();
+}
+
 __global__ void __launch_bounds__(THREADS) allreduce_kernel(const Args a) {
   __shared__ int s_e;
+  pdl_trigger();
+  pdl_wait();
   if (threadIdx.x == 0) s_e = a.epochs[blockIdx.x] + 1;
+  start_fence(a.fence_mode);  // release: earlier launches' write-backs before this launch's pushes
   __syncthreads();
   const uint64_t t0 = globaltimer_ns();
   const int par = s_e & 1;
@@ -204,7 +224,10 @@ __global__ void __launch_bounds__(THREADS) allreduce_rmsnorm_kernel(const NormAr
   const Args& a = na.b;
   __shared__ int s_e;
   __shared__ float red[THREADS / 32];
+  pdl_trigger();
+  pdl_wait();
   if (threadIdx.x == 0) s_e = a.epochs[blockIdx.x] + 1;
+  start_fence(a.fence_mode);   // release, as in allreduce_kernel
   __syncthreads();
   const uint64_t t0 = globaltimer_ns();
   const int par = s_e & 1;
@@ -367,7 +390,9 @@ void allreduce_p2p(at::Tensor& out, const at::Tensor& inp, std::vector<int64_t> 
   a.rank = static_cast<int>(rank);
   a.err = err.data_ptr<int>();
   const int g = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ctas, ar::MAX_CTAS)));
-  ar::allreduce_kernel<<<g, ar::THREADS, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  a.fence_mode = comm_fence_mode();
+  C10_CUDA_CHECK(launch_k(ar::allreduce_kernel, dim3(g), dim3(ar::THREADS), 0,
+                          at::cuda::getCurrentCUDAStream(), nullptr, 0, a));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -412,7 +437,9 @@ bool allreduce_rmsnorm_p2p(at::Tensor& h, const at::Tensor& inp, at::Tensor& x,
   na.HV = static_cast<int>(H / 8);
   na.eps = static_cast<float>(eps);
   const int g = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ctas, ar::MAX_CTAS)));
-  ar::allreduce_rmsnorm_kernel<<<g, ar::THREADS, 0, at::cuda::getCurrentCUDAStream()>>>(na);
+  na.b.fence_mode = comm_fence_mode();
+  C10_CUDA_CHECK(launch_k(ar::allreduce_rmsnorm_kernel, dim3(g), dim3(ar::THREADS), 0,
+                          at::cuda::getCurrentCUDAStream(), nullptr, 0, na));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return true;
 }

@@ -102,6 +102,8 @@ __global__ void __launch_bounds__(THREADS, 2)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int seq = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+  pdl_trigger();
+  pdl_wait();   // q, the block table, lengths and the KV rows follow the previous grid
   const int kv_len = a.seq_lens[seq];
   const int* btab = a.block_tables + static_cast<size_t>(seq) * a.bt_stride;
   const int G = a.group;
@@ -400,13 +402,12 @@ void paged_decode_tma(const at::Tensor& q, const at::Tensor& k_cache, const at::
   }
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   dim3 grid(B, a.num_kv_heads, a.num_splits);
-  decode_kernel<<<grid, THREADS, SMEM, st>>>(tk, tv, a);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  C10_CUDA_CHECK(launch_k(decode_kernel, grid, dim3(THREADS), SMEM, st, nullptr, 0, tk, tv, a));
   if (a.num_splits > 1) {
     const int nrows = a.total_rows;
-    attn_combine_kernel<<<nrows, D, 0, st>>>(a.part_o, a.part_lse, a.out, a.out_row_stride, nrows,
-                                            q.size(1), a.num_splits);
-    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    C10_CUDA_CHECK(launch_k(attn_combine_kernel, dim3(nrows), dim3(D), 0, st, nullptr, 0,
+                            a.part_o, a.part_lse, a.out, a.out_row_stride, nrows,
+                            static_cast<int>(q.size(1)), a.num_splits));
   }
 }
 

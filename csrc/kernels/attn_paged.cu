@@ -119,6 +119,8 @@ __device__ __forceinline__ void load_kv_tile(bf16* sK, bf16* sV, const AttnArgs&
 
 template <bool DECODE>
 __global__ void __launch_bounds__(ATHREADS) paged_attn_kernel(const AttnArgs a) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ uint8_t smem_raw[];
   bf16* sQ = reinterpret_cast<bf16*>(smem_raw);                  // 64 x 128
   bf16* sK = sQ + 64 * AD;                                        // 2 x 64 x 128
@@ -392,6 +394,8 @@ __global__ void __launch_bounds__(ATHREADS) paged_attn_kernel(const AttnArgs a) 
 // Combine split-KV partials: out = sum_s exp2(lse_s - lse) * o_s.
 __global__ void attn_combine_kernel(const float* part_o, const float* part_lse, bf16* out,
                                     int out_row_stride, int nrows, int heads, int splits) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x;  // token * heads + head
   const int d = threadIdx.x;   // 0..127
   float mx = -INFINITY;
@@ -472,13 +476,13 @@ void paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::T
       attr = true;
     }
     dim3 grid(num_seqs, a.num_kv_heads, splits);
-    paged_attn_kernel<true><<<grid, ATHREADS, smem, st>>>(a);
+    C10_CUDA_CHECK(launch_k(paged_attn_kernel<true>, grid, dim3(ATHREADS), smem, st, nullptr, 0, a));
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     if (splits > 1) {
       const int nrows = q.size(0) * q.size(1);
-      attn_combine_kernel<<<nrows, AD, 0, st>>>(a.part_o, a.part_lse, a.out, a.out_row_stride,
-                                               nrows, q.size(1), splits);
-      C10_CUDA_KERNEL_LAUNCH_CHECK();
+      C10_CUDA_CHECK(launch_k(attn_combine_kernel, dim3(nrows), dim3(AD), 0, st, nullptr, 0,
+                              a.part_o, a.part_lse, a.out, a.out_row_stride, nrows,
+                              static_cast<int>(q.size(1)), splits));
     }
   } else {
     TORCH_CHECK(tile_seq.has_value() && tile_row0.has_value(), "prefill needs tile lists");
@@ -494,7 +498,7 @@ void paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::T
       attr = true;
     }
     dim3 grid(ntiles, a.num_kv_heads, 1);
-    paged_attn_kernel<false><<<grid, ATHREADS, smem, st>>>(a);
+    C10_CUDA_CHECK(launch_k(paged_attn_kernel<false>, grid, dim3(ATHREADS), smem, st, nullptr, 0, a));
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 }

@@ -38,6 +38,20 @@ bool allreduce_rmsnorm_p2p(at::Tensor& h, const at::Tensor& inp, at::Tensor& x,
 void allreduce_p2p(at::Tensor& out, const at::Tensor& inp, std::vector<int64_t> bases,
                    int64_t rank, int64_t n_elems, int64_t max_elems, int64_t ctas,
                    at::Tensor& err);
+int64_t rowpar_buffer_bytes(int64_t max_tokens, int64_t hidden, int64_t world);
+std::vector<int64_t> rowpar_geometry(int64_t max_tokens, int64_t hidden, int64_t world);
+void rowpar_prepare(int64_t base, int64_t max_tokens, int64_t hidden, int64_t world);
+void rowpar_norm(at::Tensor& h, const c10::optional<at::Tensor>& partial, at::Tensor& x_own,
+                 const at::Tensor& w, std::vector<int64_t> bases, int64_t rank, int64_t T,
+                 int64_t max_tokens, double eps, int64_t ctas, at::Tensor& err,
+                 int64_t trace_ptr);
+void gemm_bf16_rowpar(const at::Tensor& A, const at::Tensor& W, at::Tensor& err,
+                      std::vector<int64_t> recv1_ptrs, int64_t rank, int64_t rp_max,
+                      int64_t epoch_ptr, const c10::optional<at::Tensor>& ws, int64_t splits,
+                      int64_t trace_ptr);
+void set_pdl_launch(bool on);
+bool pdl_launch_enabled();
+void set_comm_fence_mode(int64_t mode);
 int64_t ipc_alloc(int64_t bytes);
 void ipc_free(int64_t ptr);
 at::Tensor ipc_export(int64_t ptr);
@@ -63,7 +77,8 @@ void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual, con
              at::Tensor& y, double eps);
 void rope_kv(at::Tensor& qkv, const at::Tensor& positions, const c10::optional<at::Tensor>& slots,
              const at::Tensor& cos_sin, at::Tensor& k_cache, at::Tensor& v_cache, int64_t hq,
-             int64_t hkv, at::Tensor& err);
+             int64_t hkv, at::Tensor& err, const c10::optional<at::Tensor>& q_norm,
+             const c10::optional<at::Tensor>& k_norm, int64_t norm_dim, double eps);
 void sample_tokens(const at::Tensor& logits, const at::Tensor& temperature,
                    const at::Tensor& top_k, const at::Tensor& top_p, const at::Tensor& seeds,
                    at::Tensor& out_tokens, const c10::optional<at::Tensor>& out_logprob);
@@ -98,6 +113,24 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("A"), py::arg("W"), py::arg("C"), py::arg("residual"), py::arg("mode"),
         py::arg("err"), py::arg("bt") = 0);
   m.def("allreduce_p2p", &lb::allreduce_p2p, "two-shot all-reduce over NVLink peer memory");
+  m.def("rowpar_buffer_bytes", &lb::rowpar_buffer_bytes);
+  m.def("rowpar_geometry", &lb::rowpar_geometry);
+  m.def("rowpar_prepare", &lb::rowpar_prepare);
+  m.def("rowpar_norm", &lb::rowpar_norm,
+        "row-parallel exchange: reduce own rows + residual + RMSNorm, all-gather normed rows",
+        py::arg("h"), py::arg("partial"), py::arg("x_own"), py::arg("w"), py::arg("bases"),
+        py::arg("rank"), py::arg("T"), py::arg("max_tokens"), py::arg("eps"), py::arg("ctas"),
+        py::arg("err"), py::arg("trace_ptr") = 0);
+  m.def("gemm_bf16_rowpar", &lb::gemm_bf16_rowpar,
+        "row-parallel GEMM pushing its output rows into the owners' exchange slots",
+        py::arg("A"), py::arg("W"), py::arg("err"), py::arg("recv1_ptrs"), py::arg("rank"),
+        py::arg("rp_max"), py::arg("epoch_ptr"), py::arg("ws") = py::none(),
+        py::arg("splits") = 0, py::arg("trace_ptr") = 0);
+  m.def("set_pdl", &lb::set_pdl_launch,
+        "launch the decode-path kernels with programmatic dependent launch (default on)");
+  m.def("pdl_enabled", &lb::pdl_launch_enabled);
+  m.def("set_comm_fence_mode", &lb::set_comm_fence_mode,
+        "peer-exchange launch-start fence: 1 every thread, 2 one per CTA, 0 none (measurement)");
   m.def("ipc_alloc", &lb::ipc_alloc);
   m.def("ipc_free", &lb::ipc_free);
   m.def("ipc_export", &lb::ipc_export);
@@ -114,6 +147,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding", &lb::embedding, "embedding gather");
   m.def("forward_tokens", &lb::forward_tokens, "patch input ids from the previous step's samples");
   m.def("rmsnorm", &lb::rmsnorm, "RMSNorm with optional fused residual add");
-  m.def("rope_kv", &lb::rope_kv, "RoPE + paged KV append");
+  m.def("rope_kv", &lb::rope_kv, "RoPE + paged KV append (optional per-head q/k RMSNorm)",
+        py::arg("qkv"), py::arg("positions"), py::arg("slots"), py::arg("cos_sin"),
+        py::arg("k_cache"), py::arg("v_cache"), py::arg("hq"), py::arg("hkv"), py::arg("err"),
+        py::arg("q_norm") = py::none(), py::arg("k_norm") = py::none(), py::arg("norm_dim") = 0,
+        py::arg("eps") = 1e-6);
   m.def("sample_tokens", &lb::sample_tokens, "greedy / top-k / top-p sampling");
 }

@@ -11,6 +11,9 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
+
+#include <utility>
 
 namespace lb {
 
@@ -39,6 +42,22 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 
 __device__ __forceinline__ void record_error(int* err, int code) {
   if (err != nullptr) atomicCAS(err, 0, code);
+}
+
+// ------------------------------------------------------------------------------------
+// Programmatic dependent launch (PDL).  Kernels of the decode path are launched with
+// programmatic stream serialization (launch_k below), so a kernel's CTAs may start while the
+// previous kernel on the stream is still finishing: they run their prologue (barrier init,
+// TMEM allocation, tensor-map prefetch, and in the GEMMs the first weight tiles, which no
+// kernel writes) and then pdl_wait() until the previous grid has completed and its memory is
+// visible.  Every kernel launched that way calls pdl_wait() in every thread before it reads
+// anything an earlier kernel wrote or writes anything an earlier kernel may read; without
+// the launch attribute pdl_wait() returns at once.  pdl_trigger() lets the next kernel be
+// scheduled as soon as every CTA of this one has started.
+// ------------------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -309,5 +328,59 @@ __device__ __forceinline__ float warp_max(float v) {
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
 }
+
+// ------------------------------------------------------------------------------------
+// Host: kernel launch with the PDL attribute (on unless LB_PDL=0 or set_pdl(false)).
+// ------------------------------------------------------------------------------------
+#ifndef __CUDACC_RTC__
+inline int& pdl_state() {
+  static int state = -1;   // -1: read LB_PDL on first use
+  return state;
+}
+inline bool pdl_enabled() {
+  int& s = pdl_state();
+  if (s < 0) {
+    const char* e = getenv("LB_PDL");
+    s = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return s == 1;
+}
+inline void set_pdl(bool on) { pdl_state() = on ? 1 : 0; }
+
+// Launch-start system fence of the peer-memory exchanges (allreduce.cu, tp_rowpar.cu):
+// 0 = none (default: slot reuse is ordered by stream order, see tp_rowpar.cu), 1 = every
+// thread, 2 = one thread per CTA before a CTA barrier.  LB_COMM_FENCE overrides the default.
+inline int& comm_fence_mode() {
+  static int mode = [] {
+    const char* e = getenv("LB_COMM_FENCE");
+    return (e != nullptr && (e[0] == '1' || e[0] == '2')) ? e[0] - '0' : 0;
+  }();
+  return mode;
+}
+
+// cudaLaunchKernelEx with programmatic stream serialization (plus extra attributes, e.g. a
+// cluster dimension).  Returns the launch status.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                            cudaStream_t st, const cudaLaunchAttribute* extra, int n_extra,
+                            Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[4];
+  int n = 0;
+  for (int i = 0; i < n_extra && n < 3; ++i) attr[n++] = extra[i];
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+#endif
 
 }  // namespace lb

@@ -47,6 +47,14 @@ enum EpiMode : int { kEpiStore = 0, kEpiSwiGLU = 1, kEpiF32 = 2 };
 // and the last CTA resets the flag.  Producer side (scatter): output row m goes to owner
 // o = m / rows_per_rank, into o's reduce-scatter slot for this rank, by P2P stores; the last
 // CTA then increments every owner's flag (system-scope release).
+//
+// Push mode (push = 1, tp_rowpar.cu's exchange): the receive slots hold a sentinel until written
+// and the data is its own flag, so there are no signals and no completion counter.  Token m goes
+// to owner o = m / rows_per_rank, row m - o * rows_per_rank of slot (parity, src_rank) of o's
+// receive buffer, parity = *epoch & 1 (the exchange's counter, advanced by the consuming
+// rowpar_norm launch).  bf16 lanes equal to the sentinel 0xFFFF are sent as 0x7FFF; with the
+// optional slot-reuse fence (push = 2) every epilogue thread executes fence.acq_rel.sys at
+// kernel start.
 struct TpLink {
   bf16* scatter[8];
   int* signal[8];
@@ -57,6 +65,9 @@ struct TpLink {
   int* wait_flag;
   int wait_count;
   int* done_counter;      // local grid-completion counter (reset by the last CTA)
+  int push;               // 1: sentinel-protocol push into the row-parallel exchange (2: with
+                          // a release fence at kernel start)
+  const int* epoch;       // push mode: this rank's exchange counter (parity = epoch & 1)
 };
 
 struct GemmArgs {
@@ -223,6 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   uint32_t issued_mask = 0, issued_parity = 0;  // producer bookkeeping for abort drain
 
+  pdl_trigger();
   if (warp == 0) {
     if (lane == 0) {
       const uint64_t pw = policy_evict_first();
@@ -232,18 +244,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       WorkIter w;
       w.begin(a);
       int t, s, kb0, kb1;
-      while (!*abort_flag && w.next(a, t, s, kb0, kb1)) {
+      // The first work item's first weight tiles depend on no earlier kernel: issue them
+      // before waiting for the previous grid (PDL); their activation tiles follow the wait.
+      int pre = 0;
+      {
+        WorkIter w0 = w;
+        int t0, s0, a0, b0;
+        if (w0.next(a, t0, s0, a0, b0)) {
+          pre = min(STAGES, max(0, b0 - a0));
+          for (int i = 0; i < pre; ++i) {
+            mbar_arrive_expect_tx(&full[i], L::W_BYTES + L::X_BYTES);
+            tma_load_2d(sW + i * L::W_BYTES, &tmW, &full[i], (a0 + i) * BK,
+                        (t0 % a.n_tiles) * BW, pw);
+          }
+        }
+      }
+      pdl_wait();
+      int issued = 0;
+      while (w.next(a, t, s, kb0, kb1)) {
+        if (issued >= pre && *abort_flag) break;
         const int nt = t % a.n_tiles, mt = t / a.n_tiles;
         bool ok = true;
-        for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
-            record_error(a.err, kErrTimeoutSmemEmpty);
-            *abort_flag = 1;
-            ok = false;
-            break;
+        for (int kb = kb0; kb < kb1; ++kb, ++issued) {
+          if (issued >= pre) {
+            if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
+              record_error(a.err, kErrTimeoutSmemEmpty);
+              *abort_flag = 1;
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[stage], L::W_BYTES + L::X_BYTES);
+            tma_load_2d(sW + stage * L::W_BYTES, &tmW, &full[stage], kb * BK, nt * BW, pw);
           }
-          mbar_arrive_expect_tx(&full[stage], L::W_BYTES + L::X_BYTES);
-          tma_load_2d(sW + stage * L::W_BYTES, &tmW, &full[stage], kb * BK, nt * BW, pw);
           tma_load_2d(sX + stage * L::X_BYTES, &tmX, &full[stage], kb * BK, mt * BT, px);
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -303,6 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------- epilogue warps ----------------
+    pdl_wait();   // workspace, counters, residual and output follow the previous grid
     const int quad = warp & 3;           // TMEM lane quadrant this warp may access
     const int row = quad * 32 + lane;    // weight row within the tile == TMEM lane
     const int etid = threadIdx.x - 64;   // 0..127
@@ -562,13 +595,23 @@ namespace lb {
 
 // Destination row of output token m: local C, or (tensor-parallel scatter) the owner rank's
 // reduce-scatter receive slot for this source rank, reached by P2P stores over NVLink.
-__device__ __forceinline__ bf16* out_row(const GemmArgs& a, int m) {
+__device__ __forceinline__ bf16* out_row(const GemmArgs& a, int m, int par) {
   if (a.tp.world > 0) {
     const int o = m / a.tp.rows_per_rank;
     const int r = m - o * a.tp.rows_per_rank;
-    return a.tp.scatter[o] + a.tp.src_rank * a.tp.slot_stride + static_cast<size_t>(r) * a.ldc;
+    const long long slot = a.tp.push ? static_cast<long long>(par) * a.tp.world + a.tp.src_rank
+                                     : a.tp.src_rank;
+    return a.tp.scatter[o] + slot * a.tp.slot_stride + static_cast<size_t>(r) * a.ldc;
   }
   return reinterpret_cast<bf16*>(a.C) + static_cast<size_t>(m) * a.ldc;
+}
+
+// Push mode: a bf16 lane equal to the receive slots' sentinel 0xFFFF (a NaN) is sent as the
+// canonical NaN 0x7FFF, so a written lane can never look unwritten.
+__device__ __forceinline__ uint32_t canon_bf16x2(uint32_t w) {
+  if ((w & 0xFFFFu) == 0xFFFFu) w = (w & 0xFFFF0000u) | 0x7FFFu;
+  if ((w >> 16) == 0xFFFFu) w = (w & 0xFFFFu) | 0x7FFF0000u;
+  return w;
 }
 
 template <int BT, int STAGES>
@@ -611,6 +654,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int kb1 = min(kb0 + a.kb_per_split, a.kb_total);
   unsigned long long* tr = a.trace ? a.trace + blockIdx.x * 8 : nullptr;
   if (tr && threadIdx.x == 0) tr[0] = globaltimer_ns();
+  // Push mode: release/acquire at system scope for everything of earlier launches on this
+  // stream (the exchange's sentinel write-backs and polls) before this launch's peer stores.
+  // Issued at kernel start by the epilogue threads (the only ones that push), where it has
+  // no stores of its own to wait for and overlaps the main loop.
+  if (a.tp.push == 2 && threadIdx.x >= 64) asm volatile("fence.acq_rel.sys;" ::: "memory");
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -639,12 +687,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   bool mma_issued = false;
   if (tr && threadIdx.x == 0) tr[1] = globaltimer_ns();
 
+  pdl_trigger();
   if (warp == 0) {
     if (lane == 0) {
       const uint64_t pw = policy_evict_first();
       const uint64_t px = policy_evict_last();
       int stage = 0;
       uint32_t phase = 0;
+      // The weight tiles of the first stages depend on no earlier kernel: issue them before
+      // waiting for the previous grid (PDL), the activation tiles after.
+      const int pre = min(STAGES, max(0, kb1 - kb0));
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], L::W_BYTES + L::X_BYTES);
+        tma_load_2d(sW + i * L::W_BYTES, &tmW, &full[i], (kb0 + i) * BK, nt * BW, pw);
+      }
+      pdl_wait();
       if (a.tp.wait_flag != nullptr) {
         if (!wait_flag_geq(a.tp.wait_flag, a.tp.wait_count, abort_flag)) {
           record_error(a.err, kErrTimeoutPeer);
@@ -653,14 +710,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         // peers' rows were observed through the generic proxy; TMA reads via the async proxy
         asm volatile("fence.proxy.async.global;" ::: "memory");
       }
-      for (int kb = kb0; kb < kb1 && !*abort_flag; ++kb) {
-        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
-          record_error(a.err, kErrTimeoutSmemEmpty);
-          *abort_flag = 1;
-          break;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        const int i = kb - kb0;
+        if (i >= pre) {
+          if (*abort_flag) break;
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
+            record_error(a.err, kErrTimeoutSmemEmpty);
+            *abort_flag = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], L::W_BYTES + L::X_BYTES);
+          tma_load_2d(sW + stage * L::W_BYTES, &tmW, &full[stage], kb * BK, nt * BW, pw);
         }
-        mbar_arrive_expect_tx(&full[stage], L::W_BYTES + L::X_BYTES);
-        tma_load_2d(sW + stage * L::W_BYTES, &tmW, &full[stage], kb * BK, nt * BW, pw);
+        // prefetched stages still get their activation tile (after an abort too: the stage's
+        // barrier expects both, and the unwind below waits for every issued stage)
         tma_load_2d(sX + stage * L::X_BYTES, &tmX, &full[stage], kb * BK, mt * BT, px);
         issued_mask |= 1u << stage;
         issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -701,6 +764,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // Epilogue warps: wait for the accumulator, publish the partial tile.
+    pdl_wait();   // the split-K workspace, residual and output follow the previous grid
     const int etid = threadIdx.x - 64;
     if (etid == 0) {
       int go = 1;
@@ -736,6 +800,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       : a.mode == kEpiF32  ? crs::kOutF32
                                            : crs::kOutBf16;
     const int x0 = omode == crs::kOutSwiGLU ? nt * 64 : nt * BW;
+    const int par = a.tp.push ? (*a.tp.epoch & 1) : 0;
     // lane l: weight rows 4 l .. +3 of the chunk's token columns t0 .. t0 + 15 (acc[j])
     auto epi = [&](int oc, int t0, int l, float4 (&acc)[crs::CW]) {
       if (a.tma_out) {
@@ -764,7 +829,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint2 pk;
             pk.x = pack_bf16x2(silu(acc[j].x) * up.x, silu(acc[j].y) * up.y);
             pk.y = pack_bf16x2(silu(acc[j].z) * up.z, silu(acc[j].w) * up.w);
-            *reinterpret_cast<uint2*>(out_row(a, m) + f) = pk;
+            *reinterpret_cast<uint2*>(out_row(a, m, par) + f) = pk;
           }
           continue;
         }
@@ -778,7 +843,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (n + u < a.N) C[n + u] = vv[u];
           continue;
         }
-        bf16* C = out_row(a, m);
+        bf16* C = out_row(a, m, par);
         if (a.residual != nullptr) {
           const bf16* R = a.residual + static_cast<size_t>(m) * a.ldr;
 #pragma unroll
@@ -789,6 +854,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint2 pk;
           pk.x = pack_bf16x2(vv[0], vv[1]);
           pk.y = pack_bf16x2(vv[2], vv[3]);
+          if (a.tp.push) {
+            pk.x = canon_bf16x2(pk.x);
+            pk.y = canon_bf16x2(pk.y);
+          }
           *reinterpret_cast<uint2*>(C + n) = pk;
         } else {
 #pragma unroll
@@ -920,8 +989,8 @@ static void launch_bt(const CUtensorMap& tw, const CUtensorMap& tx, const GemmAr
                          L::TOTAL);
     attr = true;
   }
-  gemm_tc_kernel<BT, STAGES><<<grid, kThreads, L::TOTAL, st>>>(tw, tx, a);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  C10_CUDA_CHECK(launch_k(gemm_tc_kernel<BT, STAGES>, dim3(grid), dim3(kThreads), L::TOTAL, st,
+                          nullptr, 0, tw, tx, a));
 }
 
 static int pick_bt(int M) {
@@ -1025,19 +1094,13 @@ static void launch_cluster(const CUtensorMap& tw, const CUtensorMap& tx, const C
                          cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
     attr_set = true;
   }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.m_tiles * a.n_tiles * S);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = L::TOTAL;
-  cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = S;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_tc_cluster_kernel<BT, STAGES>, tw, tx, tc, a));
+  C10_CUDA_CHECK(launch_k(gemm_tc_cluster_kernel<BT, STAGES>, dim3(a.m_tiles * a.n_tiles * S),
+                          dim3(kThreads), L::TOTAL, st, attr, 1, tw, tx, tc, a));
 }
 
 // SM-pair persistent GEMM (gemm_tc2.cuh): 256-row weight tiles, clusters of 2 CTAs.
@@ -1344,6 +1407,74 @@ void gemm_bf16_tp(const at::Tensor& A, const at::Tensor& W, at::Tensor& C, int64
   std::memset(&tc, 0, sizeof(tc));
   a.tma_out =
       (a.tp.world == 0 && make_tmap_out(C, mode, M, N, crs::out_box_rows(BT, S), &tc)) ? 1 : 0;
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  switch (BT) {
+    case 16: launch_cluster<16, 8>(tw, tx, tc, a, S, st); break;
+    case 32: launch_cluster<32, 8>(tw, tx, tc, a, S, st); break;
+    case 64: launch_cluster<64, 8>(tw, tx, tc, a, S, st); break;
+    case 128: launch_cluster<128, 6>(tw, tx, tc, a, S, st); break;
+    default: launch_cluster<256, 4>(tw, tx, tc, a, S, st); break;
+  }
+}
+
+// Row-parallel GEMM of a tensor-parallel layer (o_proj / down_proj) whose epilogue pushes every
+// output row straight into its owner's receive slot of the row-parallel exchange (tp_rowpar.cu):
+// recv1_ptrs[j] = rank j's recv1 base (parity 0), slots of rp_max rows x N columns, rows owned in
+// ranges of ceil(M / world).  The exchange's rowpar_norm (partial = None) consumes them.
+void gemm_bf16_rowpar(const at::Tensor& A, const at::Tensor& W, at::Tensor& err,
+                      std::vector<int64_t> recv1_ptrs, int64_t rank, int64_t rp_max,
+                      int64_t epoch_ptr, const c10::optional<at::Tensor>& ws, int64_t splits,
+                      int64_t trace_ptr) {
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && W.scalar_type() == at::kBFloat16, "bf16");
+  TORCH_CHECK(A.stride(1) == 1 && W.stride(1) == 1, "inner stride 1");
+  const int M = A.size(0), K = A.size(1), N = W.size(0);
+  const int world = static_cast<int>(recv1_ptrs.size());
+  TORCH_CHECK(W.size(1) == K && K % 8 == 0, "gemm_rowpar: K");
+  TORCH_CHECK(world >= 2 && world <= 8 && rank >= 0 && rank < world, "gemm_rowpar: world");
+  TORCH_CHECK(N % 8 == 0, "gemm_rowpar: N % 8 == 0 (16-byte rows)");
+  const int rp = (M + world - 1) / world;
+  TORCH_CHECK(rp <= rp_max, "gemm_rowpar: tokens exceed the exchange capacity");
+  TORCH_CHECK(epoch_ptr != 0, "gemm_rowpar: epoch pointer");
+  if (M == 0) return;
+  for (int64_t p : recv1_ptrs) TORCH_CHECK(p % 16 == 0, "gemm_rowpar: 16-byte aligned slots");
+  const int BT = pick_bt(M);
+  const int m_tiles = (M + BT - 1) / BT, n_tiles = (N + BW - 1) / BW;
+  const int kb_total = (K + BK - 1) / BK;
+  int S = splits > 0 ? static_cast<int>(splits) : pick_cluster(BT, m_tiles * n_tiles, kb_total);
+  S = std::max(1, std::min(S, std::min(8, kb_total)));
+  while (S > 1 && !cluster_fits(BT, S)) --S;
+  const bool have_ws = ws.has_value() && ws->defined();
+  while (S > 1 && (!have_ws || ws->numel() < crs::ws_floats(m_tiles * n_tiles, BT, S))) --S;
+  GemmArgs a = {};
+  a.ws = S > 1 ? ws->data_ptr<float>() : nullptr;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.m_tiles = m_tiles;
+  a.n_tiles = n_tiles;
+  a.splits = 1;
+  a.kb_per_split = (kb_total + S - 1) / S;
+  a.kb_total = kb_total;
+  a.C = reinterpret_cast<void*>(recv1_ptrs[rank]);
+  a.ldc = N;
+  a.mode = kEpiStore;
+  a.err = err.data_ptr<int>();
+  a.vec_ok = 1;
+  a.tp.world = world;
+  for (int i = 0; i < world; ++i) a.tp.scatter[i] = reinterpret_cast<bf16*>(recv1_ptrs[i]);
+  a.tp.rows_per_rank = rp;
+  a.tp.src_rank = static_cast<int>(rank);
+  a.tp.slot_stride = rp_max * static_cast<long long>(N);
+  a.tp.push = comm_fence_mode() != 0 ? 2 : 1;   // 2: with the optional slot-reuse fence
+  a.tp.epoch = reinterpret_cast<const int*>(epoch_ptr);
+  a.tma_out = 0;
+  a.trace = reinterpret_cast<unsigned long long*>(trace_ptr);
+  const CUtensorMap tw = make_tmap_bf16_2d(W.data_ptr(), K, N, W.stride(0) * 2, BK, BW,
+                                           CU_TENSOR_MAP_SWIZZLE_128B);
+  const CUtensorMap tx = make_tmap_bf16_2d(A.data_ptr(), K, M, A.stride(0) * 2, BK, BT,
+                                           CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tc;
+  std::memset(&tc, 0, sizeof(tc));
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   switch (BT) {
     case 16: launch_cluster<16, 8>(tw, tx, tc, a, S, st); break;

@@ -46,6 +46,8 @@ template <int MT>
 __global__ void __launch_bounds__(WARPS * 32) gemv_kernel(
     const bf16* __restrict__ x, int ldx, const bf16* __restrict__ w, int ldw, int N, int K,
     void* y, int ldy, const bf16* __restrict__ res, int ldr, int mode, int tasks) {
+  pdl_trigger();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int task = blockIdx.x * WARPS + warp;
   if (task >= tasks) return;                 // whole warp: the shuffles below stay full
@@ -162,10 +164,10 @@ void gemv_bf16(const at::Tensor& A, const at::Tensor& W, at::Tensor& C,
   const int grid = (tasks + gv::WARPS - 1) / gv::WARPS;
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
 #define LB_GEMV(MT)                                                                        \
-  gv::gemv_kernel<MT><<<grid, gv::WARPS * 32, 0, st>>>(                                   \
-      reinterpret_cast<const bf16*>(A.data_ptr()), A.stride(0),                            \
+  C10_CUDA_CHECK(launch_k(gv::gemv_kernel<MT>, dim3(grid), dim3(gv::WARPS * 32), 0, st,    \
+      nullptr, 0, reinterpret_cast<const bf16*>(A.data_ptr()), A.stride(0),                \
       reinterpret_cast<const bf16*>(W.data_ptr()), W.stride(0), N, K, C.data_ptr(),        \
-      C.stride(0), res, ldr, static_cast<int>(mode), tasks)
+      C.stride(0), res, ldr, static_cast<int>(mode), tasks))
   switch (M) {
     case 1: LB_GEMV(1); break;
     case 2: LB_GEMV(2); break;

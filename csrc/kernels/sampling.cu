@@ -60,6 +60,8 @@ __device__ __forceinline__ uint64_t mass_fx(float x, float mx) {
 __global__ void __launch_bounds__(SThreads) sample_kernel(
     const float* logits, int ld, int vocab, const float* temperature, const int* top_k,
     const float* top_p, const int64_t* seeds, int* out_tokens, float* out_logprob) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x;
   const float* x = logits + static_cast<size_t>(row) * ld;
   const float T = temperature[row];
@@ -266,11 +268,12 @@ void sample_tokens(const at::Tensor& logits, const at::Tensor& temperature,
   if (B == 0) return;
   float* lp = nullptr;
   if (out_logprob.has_value() && out_logprob->defined()) lp = out_logprob->data_ptr<float>();
-  sample_kernel<<<B, SThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
-      logits.data_ptr<float>(), logits.stride(0), logits.size(1), temperature.data_ptr<float>(),
-      top_k.data_ptr<int>(), top_p.data_ptr<float>(), seeds.data_ptr<int64_t>(),
-      out_tokens.data_ptr<int>(), lp);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  C10_CUDA_CHECK(launch_k(sample_kernel, dim3(B), dim3(SThreads), 0,
+                          at::cuda::getCurrentCUDAStream(), nullptr, 0,
+                          logits.data_ptr<float>(), static_cast<int>(logits.stride(0)),
+                          static_cast<int>(logits.size(1)), temperature.data_ptr<float>(),
+                          top_k.data_ptr<int>(), top_p.data_ptr<float>(),
+                          seeds.data_ptr<int64_t>(), out_tokens.data_ptr<int>(), lp));
 }
 
 }  // namespace lb

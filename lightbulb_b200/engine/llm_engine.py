@@ -244,14 +244,18 @@ class LLMEngine:
         """Enable the configured peer-memory collective before any CUDA graph is captured
         (every rank takes the same steps: the setup exchanges IPC handles)."""
         mode = cfg.parallel.comm
-        if mode == "p2p" and comm.p2p_ar is None and not getattr(comm, "fused_requested", False):
-            rows = min(4096, max(cfg.scheduler.max_num_seqs, cfg.scheduler.max_num_batched_tokens))
-            comm.enable_p2p_allreduce(rows * cfg.model.hidden_size, dev)
-        elif mode == "fused" and not getattr(comm, "fused_requested", False):
+        busy = getattr(comm, "fused_requested", False) or comm.p2p_ar is not None or \
+            getattr(comm, "rowpar", None) is not None
+        rows = max(cfg.scheduler.max_num_seqs, cfg.scheduler.max_num_batched_tokens)
+        if mode == "p2p" and not busy:
+            comm.enable_rowpar(min(16384, rows), cfg.model.hidden_size, dev)
+        elif mode == "allreduce" and not busy:
+            comm.enable_p2p_allreduce(min(4096, rows) * cfg.model.hidden_size, dev)
+        elif mode == "fused" and not busy:
             from ..parallel.fused import enable_fused
             enable_fused(comm)
-        elif mode not in ("p2p", "fused", "nccl"):
-            raise ValueError(f"parallel.comm must be p2p, fused or nccl, not {mode!r}")
+        elif mode not in ("p2p", "allreduce", "fused", "nccl"):
+            raise ValueError(f"parallel.comm must be p2p, allreduce, fused or nccl, not {mode!r}")
 
     def has_runnable(self) -> bool:
         """Work that can make progress (requests paused on a tool call wait for a result)."""

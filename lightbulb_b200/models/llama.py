@@ -140,7 +140,7 @@ class LlamaModel:
         attn = torch.empty(T, hq * d, dtype=torch.bfloat16, device=self.device)
         for i, L in enumerate(self.layers):
             qkv = F.gemm_consume(h, L["qkv"])
-            ops.rope_kv(qkv, b.positions, b.slots, self.cos_sin, kv.k[i], kv.v[i], hq, hkv)
+            self._rope_kv(qkv, b, kv, i, L)
             q = qkv[:, :hq * d].view(T, hq, d)
             ops.paged_attention(q, kv.k[i], kv.v[i], b.block_tables, b.seq_lens, b.cu_q,
                                 attn.view(T, hq, d), self.group, decode=True,
@@ -153,10 +153,60 @@ class LlamaModel:
             F.norm_gather(nw, R, eps)
         return F.gemm_consume(h, self.w["lm_head"], mode=ops.EPI_F32)
 
+    def rowpar_ok(self, b: ForwardBatch) -> bool:
+        c = self.comm
+        X = getattr(c, "rowpar", None) if c is not None else None
+        return X is not None and self.device.type == "cuda" and X.fits(b.num_tokens)
+
+    def forward_rowpar(self, b: ForwardBatch, kv: KVCache) -> torch.Tensor:
+        """Tensor-parallel forward over the row-parallel exchange
+        (:mod:`lightbulb_b200.parallel.rowpar`): every row-parallel GEMM is followed by ONE
+        kernel that reduces this rank's token rows, adds them to its shard of the residual
+        stream, normalises them and all-gathers the normalised rows; decode-sized batches push
+        the GEMM output straight from its epilogue into the owners' receive slots."""
+        from ..parallel.rowpar import owned_rows
+        cfg = self.cfg
+        X = self.comm.rowpar
+        T = b.num_tokens
+        hq, hkv, d = self.hq, self.hkv, self.d
+        eps = cfg.rms_norm_eps
+        x = ops.embedding(b.input_ids, self.w["embed"])      # every row; only own rows kept
+        h = ops.rmsnorm(x, self.layers[0]["ln_in"], eps)
+        r0, n = owned_rows(T, X.world, X.rank)
+        x_own = x[r0:r0 + n]                                  # this rank's residual rows
+        attn = torch.empty(T, hq * d, dtype=torch.bfloat16, device=self.device)
+        nd = b.num_decode
+        nl = len(self.layers)
+        for i, L in enumerate(self.layers):
+            qkv = ops.gemm(h, L["qkv"])
+            self._rope_kv(qkv, b, kv, i, L)
+            q = qkv[:, :hq * d].view(T, hq, d)
+            a3 = attn.view(T, hq, d)
+            if nd > 0:
+                ops.paged_attention(q, kv.k[i], kv.v[i], b.block_tables[:nd], b.seq_lens[:nd],
+                                    b.cu_q[:nd + 1], a3, self.group, decode=True,
+                                    num_splits=b.decode_splits, scale=self.scale,
+                                    seq_lens_cpu=b.seq_lens_cpu, cu_q_cpu=b.cu_q_cpu)
+            if b.tile_seq is not None and b.tile_seq.numel() > 0:
+                ops.paged_attention(q, kv.k[i], kv.v[i], b.block_tables, b.seq_lens, b.cu_q,
+                                    a3, self.group, decode=False, tile_seq=b.tile_seq,
+                                    tile_row0=b.tile_row0, seq_lens_cpu=b.seq_lens_cpu,
+                                    cu_q_cpu=b.cu_q_cpu, scale=self.scale)
+            if self.h2o is not None and nd > 0 and i == nl - 1:
+                self.h2o.accumulate(q[:nd], kv.k[i], b.block_tables[:nd], b.seq_lens[:nd])
+            h = X.gemm_norm(attn, L["o"], x_own, L["ln_post"], eps)
+            act = ops.gemm(h, L["gate_up"], mode=ops.EPI_SWIGLU)
+            nw = self.layers[i + 1]["ln_in"] if i + 1 < nl else self.w["norm"]
+            h = X.gemm_norm(act, L["down"], x_own, nw, eps)
+        hl = h.index_select(0, b.logits_idx) if b.logits_idx.numel() != T else h
+        return ops.gemm(hl, self.w["lm_head"], mode=ops.EPI_F32)
+
     def forward(self, b: ForwardBatch, kv: KVCache) -> torch.Tensor:
         """Returns fp32 logits [len(b.logits_idx), vocab_local]."""
         if self.fused_ok(b):
             return self.forward_fused(b, kv)
+        if self.rowpar_ok(b):
+            return self.forward_rowpar(b, kv)
         return self.forward_stage(b, kv)
 
     def forward_stage(self, b: ForwardBatch, kv: KVCache, x_in: Optional[torch.Tensor] = None,
@@ -181,7 +231,7 @@ class LlamaModel:
         nd = b.num_decode
         for i, L in enumerate(self.layers):
             qkv = ops.gemm(h, L["qkv"])
-            ops.rope_kv(qkv, b.positions, b.slots, self.cos_sin, kv.k[i], kv.v[i], hq, hkv)
+            self._rope_kv(qkv, b, kv, i, L)
             q = qkv[:, :hq * d].view(T, hq, d)
             a3 = attn.view(T, hq, d)
             if nd > 0:
@@ -215,6 +265,13 @@ class LlamaModel:
             return x
         hl = h.index_select(0, b.logits_idx) if b.logits_idx.numel() != T else h
         return ops.gemm(hl, self.w["lm_head"], mode=ops.EPI_F32)
+
+    def _rope_kv(self, qkv: torch.Tensor, b: ForwardBatch, kv: KVCache, i: int, L) -> None:
+        """RoPE + paged KV append of layer ``i`` (with Qwen3's per-head q/k RMSNorm when the
+        layer carries ``q_norm`` / ``k_norm``)."""
+        ops.rope_kv(qkv, b.positions, b.slots, self.cos_sin, kv.k[i], kv.v[i], self.hq,
+                    self.hkv, q_norm=L.get("q_norm"), k_norm=L.get("k_norm"),
+                    norm_dim=self.cfg.head_dim, eps=self.cfg.rms_norm_eps)
 
     def _ones(self, n: int) -> torch.Tensor:
         t = getattr(self, "_ones_cache", None)

@@ -49,6 +49,7 @@ class TPComm:
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.fused = None  # set by parallel.fused when peer-memory kernels are enabled
         self.p2p_ar = None  # two-shot peer-memory all-reduce (parallel/allreduce.py)
+        self.rowpar = None  # row-parallel exchange: reduce + residual + norm + gather (rowpar.py)
         # one-kernel all-reduce + residual + RMSNorm; off by default: measured at TP2 (256 x
         # 4096) 14.0 us against 8.4 + 4.1 us for the all-reduce and the norm kernel
         self.fuse_norm = False
@@ -65,6 +66,15 @@ class TPComm:
             dev = device or torch.device("cuda", torch.cuda.current_device())
             self.p2p_ar = P2PAllReduce(self, max_elems, dev)
         return self.p2p_ar
+
+    def enable_rowpar(self, max_tokens: int, hidden: int, device=None):
+        """Use the row-parallel exchange (one kernel per row-parallel sub-layer output, the
+        GEMM epilogue pushing into it for decode-sized batches) for up to ``max_tokens`` rows."""
+        if self.world > 1 and self.rowpar is None:
+            from .rowpar import RowParallelExchange
+            dev = device or torch.device("cuda", torch.cuda.current_device())
+            self.rowpar = RowParallelExchange(self, max_tokens, hidden, dev)
+        return self.rowpar
 
     def gemm_all_reduce(self, a: torch.Tensor, w) -> torch.Tensor:
         """``a @ w.T`` summed over ranks (row-parallel layer): the GEMM writes straight into
@@ -95,6 +105,10 @@ class TPComm:
             torch.cuda.synchronize()
             self.p2p_ar.close()
             self.p2p_ar = None
+        if self.rowpar is not None:
+            torch.cuda.synchronize()
+            self.rowpar.close()
+            self.rowpar = None
 
     def min_int(self, v: int) -> int:
         if self.world == 1:

@@ -111,6 +111,91 @@ def main(argv=None) -> int:
         ops.gemm(hh, Wgu, mode=ops.EPI_SWIGLU)
 
     res["p2p_norm_chain_us"] = timed(p2p_norm_chain)
+    # row-parallel exchange (default TP path): o_proj and down_proj, pushing GEMM epilogue or
+    # local partial, each followed by reduce + residual + RMSNorm + all-gather in one kernel
+    X = comm.enable_rowpar(max(512, T), H, dev)
+    from .rowpar import owned_rows
+    r0, nown = owned_rows(T, world, rank)
+    xo = x.clone()[r0:r0 + nown].contiguous()
+    hbuf = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    fd = a.ffn // world
+    Wd = (torch.randn(H, fd, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    act = torch.randn(T, fd, device=dev, generator=g).to(torch.bfloat16)
+    res["rowpar_norm_local_us"] = timed(lambda: X.norm(o, xo, lnw, T, 1e-5, out=hbuf))
+
+    def rp_push(inp, w):
+        X.gemm(inp, w)
+        X.norm(None, xo, lnw, T, 1e-5, out=hbuf)
+
+    def rp_local(inp, w):
+        X.norm(ops.gemm(inp, w), xo, lnw, T, 1e-5, out=hbuf)
+
+    res["rowpar_push_o_us"] = timed(lambda: rp_push(attn, Wo))
+    res["rowpar_local_o_us"] = timed(lambda: rp_local(attn, Wo))
+    res["rowpar_push_down_us"] = timed(lambda: rp_push(act, Wd))
+    res["rowpar_local_down_us"] = timed(lambda: rp_local(act, Wd))
+    res["gemm_down_local_us"] = timed(lambda: ops.gemm(act, Wd))
+
+    def rp_chain():
+        rp_push(attn, Wo)
+        ops.gemm(hbuf, Wgu, mode=ops.EPI_SWIGLU)
+
+    res["rowpar_chain_us"] = timed(rp_chain)
+
+    def rp_layer():
+        # one decode layer's comm-relevant chain: o_proj -> exchange -> gate_up -> down ->
+        # exchange (local-partial mode, the default)
+        rp_local(attn, Wo)
+        a2 = ops.gemm(hbuf, Wgu, mode=ops.EPI_SWIGLU)
+        X.norm(ops.gemm(a2, Wd), xo, lnw, T, 1e-5, out=hbuf)
+
+    for mode in (1, 2, 0):
+        X.C.set_comm_fence_mode(mode)
+        res[f"rowpar_norm_local_fence{mode}_us"] = timed(lambda: X.norm(o, xo, lnw, T, 1e-5,
+                                                                         out=hbuf))
+        res[f"p2p_allreduce_fence{mode}_us"] = timed(lambda: ar(xin))
+    X.C.set_comm_fence_mode(1)
+    for on in (True, False):
+        X.C.set_pdl(on)
+        res[f"rowpar_layer_pdl{int(on)}_us"] = timed(rp_layer)
+    X.C.set_pdl(True)
+    # roofline of GEMM + exchange: the slower of tensor FLOPs at the measured GEMM peak,
+    # HBM bytes (weights) at the measured copy bandwidth, and bytes leaving this rank over
+    # NVLink (partials to owners + normalised rows to every peer) at 770 GB/s per direction
+    from ..utils.microbench import peaks
+    hbm, tflops, _src = peaks()
+    nvl = 2 * (world - 1) / world * T * H * 2
+    for name, k in (("o", qd), ("down", fd)):
+        fl = 2 * T * k * H
+        roof = max(fl / tflops, H * k * 2 / hbm, nvl / 770e9) * 1e6
+        res[f"rowpar_{name}_roofline_us"] = roof
+        res[f"rowpar_push_{name}_frac_of_roofline"] = roof / res[f"rowpar_push_{name}_us"]
+    # one traced push + exchange (globaltimer ns relative to this rank's GEMM start): GEMM CTA
+    # stamps [start, setup, acc ready, published, cluster synced, reduced+stored, done], exchange
+    # CTA 0 [start, pushed, own rows done, gathered]
+    tr_g = torch.zeros(4096 * 8, dtype=torch.int64, device=dev)
+    tr_x = torch.zeros(8, dtype=torch.int64, device=dev)
+    torch.cuda.synchronize()
+    comm.barrier()
+    X.C.gemm_bf16_rowpar(attn, Wo, X.err, X.recv1, rank, X.rp_max, X.epoch_ptr, X.ws, 0,
+                         tr_g.data_ptr())
+    X.C.rowpar_norm(hbuf, None, xo, lnw, X.bases, rank, T, X.max_tokens, 1e-5, X.ctas, X.err,
+                    tr_x.data_ptr())
+    torch.cuda.synchronize()
+    gg = tr_g.view(-1, 8).cpu()
+    used = gg[:, 0] > 0
+    g0 = int(gg[used, 0].min())
+    xx = tr_x.cpu().tolist()
+    rtrace = {"gemm_last_start": int(gg[used, 0].max()) - g0,
+              "gemm_acc_ready_max": int(gg[used, 2].max()) - g0,
+              "gemm_synced_max": int(gg[used, 4].max()) - g0,
+              "gemm_stored_max": int(gg[used, 5].max()) - g0,
+              "gemm_done_max": int(gg[used, 6].max()) - g0,
+              "x_start": xx[0] - g0, "x_pushed": xx[1] - g0, "x_own_done": xx[2] - g0,
+              "x_gathered": xx[3] - g0}
+    tall = [None] * world
+    dist.all_gather_object(tall, rtrace)
+    res["rowpar_trace_ns"] = tall
     o2 = ops.gemm(attn, Wo)               # o itself was all-reduced in place by the timing above
     ref = o2.float().clone()
     dist.all_reduce(ref)

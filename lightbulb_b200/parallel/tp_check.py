@@ -1,6 +1,6 @@
 """Tensor-parallel self-check (run under torchrun, one process per GPU).
 
-    torchrun --nproc-per-node N -m lightbulb_b200.parallel.tp_check [--comm nccl|fused|p2p]
+    torchrun --nproc-per-node N -m lightbulb_b200.parallel.tp_check [--comm nccl|fused|p2p|allreduce]
 
 Every rank builds the same random-init model sharded over the ranks and greedily generates;
 rank 0 also runs the unsharded model on its own GPU and compares.  Exit code 0 = match.
@@ -16,7 +16,7 @@ import torch.distributed as dist
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--comm", default="nccl", choices=["nccl", "fused", "p2p"])
+    ap.add_argument("--comm", default="nccl", choices=["nccl", "fused", "p2p", "allreduce"])
     ap.add_argument("--graphs", type=int, default=1)
     args = ap.parse_args(argv)
     from ..config import CacheConfig, EngineConfig, ParallelConfig, SchedulerConfig, get_preset

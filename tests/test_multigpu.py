@@ -34,7 +34,14 @@ def test_p2p_allreduce_two_ranks():
 
 
 @pytest.mark.skipif(_ngpus() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("comm", ["p2p", "nccl"])
+def test_rowpar_exchange_two_ranks():
+    r = _torchrun("lightbulb_b200.parallel.rowpar", port=29633)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "ok" in r.stdout
+
+
+@pytest.mark.skipif(_ngpus() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("comm", ["p2p", "allreduce", "nccl"])
 def test_tp2_generation_matches_oracle(comm):
     r = _torchrun("lightbulb_b200.parallel.tp_check", "--comm", comm, port=29632)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]

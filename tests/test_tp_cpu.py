@@ -119,3 +119,17 @@ def test_argmax_vocab_parallel_first_max():
     for rank, got, ref in res:
         assert not isinstance(got, str), got
         assert got == ref and got[1] == 7 and got[3] == 12
+
+
+def test_rowpar_owned_rows_partition():
+    # token rows are owned in contiguous ranges of ceil(T / world); every row exactly once,
+    # ranks past the end own nothing (e.g. 3 tokens on 8 ranks)
+    from lightbulb_b200.parallel.rowpar import owned_rows
+    for world in (2, 3, 4, 8):
+        for T in (1, 3, 7, 8, 255, 256, 257, 640):
+            seen = []
+            for r in range(world):
+                r0, n = owned_rows(T, world, r)
+                assert n >= 0 and (n == 0 or r0 + n <= T)
+                seen += list(range(r0, r0 + n))
+            assert seen == list(range(T))
