@@ -240,6 +240,47 @@ def test_sampling_greedy_and_topk_topp():
     assert logits[2, o[2]] >= kth
 
 
+@pytest.mark.parametrize("k,p,t", [(1, 1.0, 0.7), (5, 0.9, 1.0), (50, 0.9, 0.8), (50, 0.5, 1.3),
+                                   (1000, 0.95, 1.0), (4000, 1.0, 0.6), (20, 0.3, 2.0)])
+def test_sampling_candidate_path_matches_reference(k, p, t):
+    # top-k rows take the two-pass candidate path; every row must equal the CPU restatement
+    # (same thresholds, same seeded index-order draw) and be deterministic across launches
+    from lightbulb_b200.engine.sampling import sample_row_reference
+    g = torch.Generator().manual_seed(k + int(100 * p))
+    B, V = 8, 128256
+    logits = torch.randn(B, V, generator=g) * 3
+    logits[3, 100:140] = 9.0          # a tie group straddling the top-k boundary
+    logits[5] = (torch.randn(V, generator=g) * 3).round()   # heavy ties everywhere
+    lg = logits.to(DEV)
+    temp = torch.full((B,), t, device=DEV)
+    topk = torch.full((B,), k, dtype=torch.int32, device=DEV)
+    topp = torch.full((B,), p, device=DEV)
+    seeds = torch.arange(11, 11 + B, dtype=torch.int64, device=DEV)
+    out = ops.sample(lg, temp, topk, topp, seeds)
+    out2 = ops.sample(lg, temp, topk, topp, seeds)
+    torch.cuda.synchronize()
+    assert torch.equal(out, out2)
+    for r in range(B):
+        exp = sample_row_reference(logits[r], t, k, p, 11 + r)
+        assert int(out[r]) == exp, (r, int(out[r]), exp)
+
+
+def test_sampling_candidate_overflow_falls_back():
+    # a flat row: the k-th largest key's bin holds more candidates than shared memory takes, so
+    # the general radix path runs; result still equals the reference
+    from lightbulb_b200.engine.sampling import sample_row_reference
+    V = 128256
+    logits = torch.zeros(2, V)
+    logits[1, ::3] = 0.5
+    out = ops.sample(logits.to(DEV), torch.tensor([1.0, 1.0], device=DEV),
+                     torch.tensor([100, 30000], dtype=torch.int32, device=DEV),
+                     torch.tensor([0.9, 0.7], device=DEV),
+                     torch.tensor([5, 6], dtype=torch.int64, device=DEV))
+    torch.cuda.synchronize()
+    for r, (k, p) in enumerate([(100, 0.9), (30000, 0.7)]):
+        assert int(out[r]) == sample_row_reference(logits[r], 1.0, k, p, 5 + r)
+
+
 def test_sampling_distribution():
     V = 1000
     logits = torch.zeros(1, V, device=DEV)
