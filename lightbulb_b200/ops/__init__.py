@@ -149,6 +149,13 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
             _launches[0] += 1
             return out
         s = scratch(a.device)
+        if splits < 0:
+            # a forced cluster split-K plan must fit the shared workspace: refuse it here rather
+            # than in the extension
+            need = gemm_plan(m, n, a.shape[1], bt, splits)[3]
+            if need > s.gemm_ws.numel():
+                raise ValueError(f"gemm: cluster split-K plan (bt {bt}, splits {splits}) needs "
+                                 f"{need} workspace floats > {s.gemm_ws.numel()}")
         C.gemm_bf16(a, w, out, residual, mode, s.gemm_ws, s.gemm_counters, s.err, bt, splits,
                     None)
         _launches[0] += 1
