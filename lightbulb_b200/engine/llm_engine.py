@@ -407,6 +407,36 @@ class LLMEngine:
             raise ValueError(kind)
         return self.kv_policy
 
+    def enable_segmented_cache(self, config=None, context_limit: Optional[int] = None,
+                               segment_tokens: int = 64, knowledge_base=None):
+        """Drive segmented spans and tiered storage from the step loop (see
+        :class:`lightbulb_b200.kv.spans.SegmentedPolicy`): automatic spans, attention-scored
+        eviction under context pressure with demotion to RAM / disk and a knowledge-base fact
+        per demoted span, and ``<RETRIEVE:key>`` promotion.  Replaces any other KV policy."""
+        from ..kv.spans import SegmentedPolicy
+        self.kv_policy = SegmentedPolicy(self, config, context_limit, segment_tokens,
+                                         knowledge_base)
+        return self.kv_policy
+
+    def inject_context(self, request_id: str, text: Optional[str] = None,
+                       token_ids: Optional[List[int]] = None) -> Sequence:
+        """Append context (a system note, a retrieved document, a tool's output) to a running
+        request: the tokens are prefilled into its KV on the next step, then decoding resumes."""
+        if self._pending is not None:
+            raise RuntimeError("an overlapped decode step is in flight: inject after the "
+                               "engine drained (with a KV policy set, steps are synchronous)")
+        for seq in self.scheduler.running:
+            if seq.request_id == request_id and not seq.finished:
+                break
+        else:
+            raise KeyError(f"{request_id}: no running request")
+        ids = list(token_ids) if token_ids is not None else self.tokenizer.encode(
+            text or "", False)
+        if seq.num_tokens + len(ids) >= self.cfg.scheduler.max_model_len:
+            raise ValueError("context does not fit")
+        seq.append_context(ids)
+        return seq
+
     def _process(self, chunks, tokens) -> List[RequestOutput]:
         now = time.perf_counter()
         outs: List[RequestOutput] = []

@@ -19,6 +19,7 @@ steps).
 from __future__ import annotations
 
 import enum
+import time
 import itertools
 import logging
 from dataclasses import dataclass, field
@@ -230,12 +231,17 @@ class SegmentedEvictionPolicy:
             out.append((sid, sc.relevance))
         return sorted(out, key=lambda x: (x[1], x[0]))
 
-    def plan(self, registry: SpanRegistry, tokens_to_free: int) -> List[int]:
-        """Lowest-relevance closed spans until ``tokens_to_free`` positions are covered."""
+    def plan(self, registry: SpanRegistry, tokens_to_free: int,
+             protected: Iterable[int] = ()) -> List[int]:
+        """Lowest-relevance closed spans until ``tokens_to_free`` positions are covered
+        (spans in ``protected`` are skipped)."""
         chosen, freed = [], 0
+        skip = set(protected)
         for sid, _ in self.rank_spans_for_eviction(registry):
             if freed >= tokens_to_free:
                 break
+            if sid in skip:
+                continue
             chosen.append(sid)
             freed += sum(1 for _ in registry.get(sid).positions())
         return chosen
@@ -297,7 +303,7 @@ class SegmentedKV:
             return 0.0
         return float(h2o.score[table[pos // bs] * bs + pos % bs])
 
-    def step(self, seq, context_limit: int) -> List[int]:
+    def step(self, seq, context_limit: int, protected: Iterable[int] = ()) -> List[int]:
         reg = self.registry(seq)
         used = seq.num_computed_tokens
         self.policy.update_scores(reg, lambda p: self.attention_of(seq, p),
@@ -305,7 +311,7 @@ class SegmentedKV:
         if self.policy.smoothed_pressure <= self.cfg.eviction_pressure_threshold:
             return []
         target = int(context_limit * self.cfg.eviction_pressure_threshold)
-        spans = self.policy.plan(reg, used - target)
+        spans = self.policy.plan(reg, used - target, protected)
         if not spans:
             return []
         if self.cfg.shadow_mode:
@@ -356,3 +362,154 @@ class SegmentedKV:
             s.start -= shift_s
             s.end -= shift_e
         self.evicted_spans += len(span_ids)
+
+
+class SegmentedPolicy:
+    """Segmented spans and tiered storage driven by the engine's step loop (reference
+    ``src/model/parallel_model_manager.rs:626-660`` enable_segmented_cache and ``:689-853``
+    eviction-pressure handling with demotion).  Installed as the engine's KV policy:
+
+    * spans are created automatically: the prompt as one ``USER_INPUT`` span once prefilled,
+      the generated KV in ``MODEL_GENERATION`` segments of ``segment_tokens``;
+    * attention statistics come from the H2O score pool that the model accumulates on the device
+      in every decode step (the H2O policy's compaction is not used);
+    * after every step, each running sequence's spans are scored and, when the context
+      utilisation (KV length / ``context_limit``) stays above the pressure threshold, the
+      lowest-scoring spans are evicted (compaction kernel), demoted first to the RAM tier
+      (spilling to disk past ``max_ram_demoted_segments``) with a knowledge-base fact whose
+      ``[KB:key] summary`` placeholder names the tier key;
+    * new tokens of each sequence (generated or injected as context) are scanned for
+      ``<RETRIEVE:key>``; a named span is promoted back into the sequence's KV (appended at the
+      end, keys keep their rotary positions) and registered as a ``LONG_TERM_MEMORY`` span.
+    """
+
+    def __init__(self, engine, config: Optional[SegmentedCacheConfig] = None,
+                 context_limit: Optional[int] = None, segment_tokens: int = 64,
+                 knowledge_base=None, summarize=None):
+        from .compression import H2OPolicy
+        from .tiers import BlockTierMover, FileDiskStore, MemoryDiskStore
+        self.eng = engine
+        self.cfg = config or SegmentedCacheConfig.live()
+        self.h2o = H2OPolicy(engine, budget=1 << 30, sinks=0)     # score accumulation only
+        disk = (FileDiskStore(self.cfg.disk_storage_path) if self.cfg.disk_storage_path
+                else MemoryDiskStore())
+        self.kb = knowledge_base
+        self.summarize = summarize or self._summary
+        self.tiers = BlockTierMover(engine, disk=disk,
+                                    max_ram_entries=self.cfg.max_ram_demoted_segments,
+                                    knowledge_base=None, summarize=self.summarize)
+        self.seg = SegmentedKV(engine, self.cfg, self.tiers)
+        self.context_limit = context_limit or engine.cfg.scheduler.max_model_len
+        self.segment_tokens = int(segment_tokens)
+        self._end: Dict[int, int] = {}        # KV end covered by spans, per sequence
+        self._scanned: Dict[int, int] = {}    # tokens already scanned for RETRIEVE markers
+        self._tail: Dict[int, str] = {}       # undecoded text tail (a marker split by a step)
+        # spans that may not be evicted yet: span id -> steps of grace left.  A promoted span
+        # was asked for by the model and has no attention history yet; it gets
+        # ``segment_tokens`` decode steps to earn a score before it can be evicted again.
+        self._grace: Dict[int, Dict[int, int]] = {}
+        self.stats = {"spans": 0, "evicted_spans": 0, "demoted": 0, "promoted": 0}
+
+    def _summary(self, token_ids: List[int]) -> str:
+        ids = [t for t in token_ids if t >= 0]
+        try:
+            text = self.eng.tokenizer.decode(ids)
+        except Exception:
+            text = ""
+        text = " ".join(text.split())
+        return (text[:77] + "...") if len(text) > 80 else (text or f"{len(ids)} tokens")
+
+    def before_step(self, so) -> None:
+        self.h2o.before_step(so)
+
+    # -- span bookkeeping ---------------------------------------------------------------
+    def _register(self, seq) -> None:
+        reg = self.seg.registry(seq)
+        sid, kvlen = seq.seq_id, seq.num_computed_tokens
+        end = self._end.get(sid)
+        if end is None:
+            if kvlen < seq.prompt_len or kvlen == 0:
+                return                                      # prompt not yet in the KV
+            reg.tag_range(0, seq.prompt_len, CacheTag.USER_INPUT, "prompt")
+            self.stats["spans"] += 1
+            end = seq.prompt_len
+        while kvlen - end >= self.segment_tokens:
+            reg.tag_range(end, end + self.segment_tokens, CacheTag.MODEL_GENERATION)
+            self.stats["spans"] += 1
+            end += self.segment_tokens
+        self._end[sid] = end
+
+    def _retrieve(self, seq) -> None:
+        from .tiers import find_retrieve_requests
+        toks = seq.all_token_ids
+        start = self._scanned.get(seq.seq_id, len(seq.prompt_token_ids))
+        if start >= len(toks):
+            return
+        new = [t for t in toks[start:] if t >= 0]
+        self._scanned[seq.seq_id] = len(toks)
+        try:
+            text = self._tail.get(seq.seq_id, "") + self.eng.tokenizer.decode(new)
+        except Exception:
+            return
+        keys = find_retrieve_requests(text)
+        cut = text.rfind("<RETRIEVE:")
+        self._tail[seq.seq_id] = text[cut:] if cut >= 0 and ">" not in text[cut:] else ""
+        for key in keys:
+            if key not in self.tiers.entries:
+                continue
+            reg = self.seg.registry(seq)
+            end = self._end.get(seq.seq_id, 0)
+            kvlen = seq.num_computed_tokens
+            if kvlen > end:                      # cover the uncovered tail first
+                reg.tag_range(end, kvlen, CacheTag.MODEL_GENERATION)
+                self.stats["spans"] += 1
+            n = self.tiers.promote(seq, key)
+            span = reg.tag_range(kvlen, kvlen + n, CacheTag.LONG_TERM_MEMORY, key)
+            self._grace.setdefault(seq.seq_id, {})[span] = self.segment_tokens
+            self._end[seq.seq_id] = kvlen + n
+            self.stats["promoted"] += 1
+
+    def after_step(self, engine) -> None:
+        for seq in list(engine.scheduler.running):
+            if seq.num_uncomputed != 1:            # still prefilling: nothing settled yet
+                continue
+            self._retrieve(seq)
+            self._register(seq)
+            before_kv = seq.num_computed_tokens
+            grace = self._grace.get(seq.seq_id, {})
+            spans = self.seg.step(seq, self.context_limit, protected=list(grace))
+            for sid in list(grace):
+                grace[sid] -= 1
+                if grace[sid] <= 0:
+                    del grace[sid]
+            if spans and not self.cfg.shadow_mode:
+                self.stats["evicted_spans"] += len(spans)
+                # every evicted position lay below the covered end: it moves left as much
+                self._end[seq.seq_id] = self._end.get(seq.seq_id, 0) - \
+                    (before_kv - seq.num_computed_tokens)
+                self._record_facts(seq, spans)
+
+    def _record_facts(self, seq, span_ids: List[int]) -> None:
+        """A knowledge-base fact per demoted span, keyed by its tier key (what a
+        ``<RETRIEVE:key>`` names)."""
+        self.stats["demoted"] = self.tiers.stats["demoted"]
+        if self.kb is None:
+            return
+        from ..extras.knowledge import EvictionRecord, Fact
+        for sid in span_ids:
+            key = f"seq{seq.seq_id}-span{sid}"
+            e = self.tiers.entries.get(key)
+            if e is None or self.kb.peek_fact(key) is not None:
+                continue
+            lo, hi = (e.positions[0], e.positions[-1] + 1) if e.positions else (0, 0)
+            self.kb.add_fact(Fact(self.summarize(e.token_ids), source=f"evicted_{lo}_{hi}",
+                                  key=key, summary=e.summary or self.summarize(e.token_ids),
+                                  source_tokens=list(e.token_ids)))
+            self.kb.evictions.append(EvictionRecord(key, (lo, hi), f"[KB:{key}] {e.summary}",
+                                                    time.time()))
+
+    def placeholders(self, seq) -> List[str]:
+        """``[KB:key] summary`` lines of the spans demoted from ``seq``."""
+        return [f"[KB:{k}] {e.summary}" for k, e in self.tiers.entries.items()
+                if e.seq_id == seq.seq_id]
+
