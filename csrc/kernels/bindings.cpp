@@ -14,6 +14,11 @@ void paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::T
                      bool decode, int64_t num_splits, const c10::optional<at::Tensor>& part_o,
                      const c10::optional<at::Tensor>& part_lse, bool causal,
                      const c10::optional<at::Tensor>& err);
+void paged_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                        at::Tensor& out, const at::Tensor& block_tables, const at::Tensor& seq_lens,
+                        const at::Tensor& cu_q, const at::Tensor& tile_seq,
+                        const at::Tensor& tile_row0, int64_t group, double scale, bool causal,
+                        const c10::optional<at::Tensor>& err);
 void paged_decode_tma(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                       at::Tensor& out, const at::Tensor& block_tables, const at::Tensor& seq_lens,
                       int64_t group, double scale, int64_t num_splits,
@@ -70,6 +75,9 @@ void kv_compact(at::Tensor& storage, const at::Tensor& src, const at::Tensor& ds
 void gemm_quant(const at::Tensor& X, const at::Tensor& qw, const at::Tensor& scales,
                 const at::Tensor& offsets, int64_t bits, int64_t group, at::Tensor& C,
                 int64_t mode, int64_t splits, at::Tensor& err, at::Tensor& ws);
+void gemm_quant_iz(const at::Tensor& X, const at::Tensor& qw, const at::Tensor& scales,
+                   const at::Tensor& offsets, int64_t group, at::Tensor& C, int64_t mode,
+                   int64_t splits, at::Tensor& err, at::Tensor& ws);
 void embedding(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, at::Tensor& err);
 void forward_tokens(at::Tensor& ids, const at::Tensor& src, const at::Tensor& last,
                     at::Tensor& err);
@@ -97,6 +105,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("tile_row0"), py::arg("group"), py::arg("scale"), py::arg("decode"),
         py::arg("num_splits"), py::arg("part_o"), py::arg("part_lse"), py::arg("causal"),
         py::arg("err") = py::none());
+  m.def("paged_attention_tc", &lb::paged_attention_tc,
+        "tcgen05 paged attention for chunked prefill / verify (S, O in TMEM, P from TMEM)");
   m.def("paged_decode_tma", &lb::paged_decode_tma, "TMA-fed warp-specialised paged decode");
   m.def("gemm_bf16_tp", &lb::gemm_bf16_tp, "tensor-parallel GEMM (wait / scatter / signal)",
         py::arg("A"), py::arg("W"), py::arg("C"), py::arg("mode"), py::arg("err"),
@@ -144,6 +154,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("h2o_accumulate", &lb::h2o_accumulate, "H2O decayed attention-mass accumulation");
   m.def("kv_compact", &lb::kv_compact, "copy kept KV token slots (all layers)");
   m.def("gemm_quant", &lb::gemm_quant, "dequant-fused tcgen05 GEMM (int4 / int8 groups)");
+  m.def("gemm_quant_iz", &lb::gemm_quant_iz,
+        "small-batch 4-bit GEMM with integer zero points (weights in TMEM, per-group rescale)");
   m.def("embedding", &lb::embedding, "embedding gather");
   m.def("forward_tokens", &lb::forward_tokens, "patch input ids from the previous step's samples");
   m.def("rmsnorm", &lb::rmsnorm, "RMSNorm with optional fused residual add");

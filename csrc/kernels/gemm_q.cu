@@ -303,6 +303,320 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 }  // namespace q
 
+// ---------------------------------------------------------------------------------------------
+// Small-batch path for integer-zero 4-bit weights (AWQ: w = (q - z) * s, group >= 64), M <= 32.
+//
+// At decode batch sizes the full-dequant kernel above is bound by the dequant instructions and
+// by shared memory: every 4 KB packed k-block becomes 16 KB of bf16 written to and read back
+// from shared memory, more than the SM's shared-memory bandwidth at HBM rate.  This kernel keeps
+// the weights exact integers and moves the scale out of the inner loop:
+//
+//   y[t, n] = sum_g s[n, g] * sum_{k in g} x[t, k] * (q[n, k] - z[n, g])
+//
+//   * converter warps turn each packed word into bf16 pairs (128 + q) with one mask-or, subtract
+//     (128 + z) with one bf16x2 subtract (exact: small integers), and store the row straight into
+//     TENSOR memory with tcgen05.st -- the MMA reads its A operand (the weight tile) from TMEM, so
+//     the expanded tile never touches shared memory;
+//   * one thread issues tcgen05.mma (A from TMEM, the activation tile from shared memory) into
+//     one of two per-group accumulators in TMEM;
+//   * the same converter warps, one group behind, read a finished group accumulator (tcgen05.ld),
+//     scale it by s[n, g] in fp32 and add it to the running sum in registers, then free it.
+// The running sums go back to TMEM once, and the split-K exchange over the cluster (no
+// multicast) and the output epilogue are those of the kernel above.
+//
+// Warps: 0 TMA producer, 1 MMA issuer (+ TMEM owner), 2..9 converters: warp w handles TMEM lane
+// quarter (w & 3) and half (w - 2) >> 2 of each k-block's 64 columns / of the token columns.
+namespace qs {
+
+constexpr int BW = 128, BK = 64, THREADS = 320, NCONV = 8;
+constexpr int TMEM_COLS = 256, ACOL = 64;  // [0, 2 BT): group accumulators; [64, 256): A stages
+
+struct Args {
+  int M, N, K, n_tiles, kb_per_split, kb_total, kpg;
+  const __half* scales;   // [N, K / group]
+  const __half* offsets;  // [N, K / group] = z * s
+  int gpr;                // groups per weight row
+  int mode;               // 0 bf16, 1 swiglu, 2 fp32
+  int* err;
+  float* ws;
+};
+
+template <int BT, int STAGES>
+struct Smem {
+  static constexpr int X_BYTES = BT * BK * 2;       // 1024-aligned (BT = 16 / 32)
+  static constexpr int Q_BYTES = BW * BK / 2;       // packed 4-bit tile
+  static constexpr int STAGE = X_BYTES + Q_BYTES;
+  static constexpr int PIPE = STAGES * STAGE;
+  static constexpr int SLOTS = crs::smem_bytes(BT, 8);
+  static constexpr int DATA = PIPE > SLOTS ? PIPE : SLOTS;
+  static constexpr int BAR_OFF = DATA;
+  static constexpr int TOTAL = BAR_OFF + 512 + 1024;
+};
+
+__device__ __forceinline__ uint32_t sub_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+template <int BT, int STAGES>
+__global__ void __launch_bounds__(THREADS, 2)
+    gemm_qs_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmX,
+                   const __grid_constant__ CUtensorMap tmC, const Args a) {
+  using L = Smem<BT, STAGES>;
+  constexpr int HC = BT / 2;  // token columns per converter half
+  static_assert(ACOL >= 2 * BT && ACOL + STAGES * 32 <= TMEM_COLS, "TMEM plan");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  auto sX = [&](int s) { return smem + s * L::STAGE; };
+  auto sQ = [&](int s) { return smem + s * L::STAGE + L::X_BYTES; };
+  float* sSlots = reinterpret_cast<float*>(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* full = bars;
+  uint64_t* ready = bars + STAGES;
+  uint64_t* empty = bars + 2 * STAGES;
+  uint64_t* gfull = bars + 3 * STAGES;  // [2]
+  uint64_t* gempty = gfull + 2;         // [2]
+  uint64_t* rbar = gempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* s_go = reinterpret_cast<volatile int*>(tmem_slot + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t S = crs::nctarank(), rank = crs::ctarank();
+  const int nt = blockIdx.x / S;
+  float* ws_tile = a.ws + crs::ws_floats(nt, BT, S);
+  const int kb0 = rank * a.kb_per_split;
+  const int kb1 = min(kb0 + a.kb_per_split, a.kb_total);
+  const int ngroups = kb1 > kb0 ? (kb1 - kb0) / a.kpg : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&ready[s], NCONV);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&gfull[b], 1);
+      mbar_init(&gempty[b], NCONV);
+    }
+    mbar_init(rbar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmX);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pw = policy_evict_first(), px = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
+          record_error(a.err, kErrTimeoutSmemEmpty);
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[stage], L::Q_BYTES + L::X_BYTES);
+        tma_load_2d(sQ(stage), &tmQ, &full[stage], kb * BK / 2, nt * BW, pw);
+        tma_load_2d(sX(stage), &tmX, &full[stage], kb * BK, 0, px);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BW, BT);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        const int j = (kb - kb0) / a.kpg, r = (kb - kb0) % a.kpg;
+        if (r == 0 && !mbar_wait(&gempty[j & 1], ((j >> 1) & 1) ^ 1u, abort_flag)) {
+          record_error(a.err, kErrTimeoutTmemEmpty);
+          *abort_flag = 1;
+          break;
+        }
+        if (!mbar_wait(&ready[stage], phase, abort_flag)) {
+          record_error(a.err, kErrTimeoutTmaFull);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t xb = smem_u32(sX(stage));
+        const uint32_t acc = tmem_base + (j & 1) * BT;
+        const uint32_t at = tmem_base + ACOL + stage * 32;
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k)
+          tc_mma_f16_ts(acc, at + k * 8, sw128_kmajor_desc(xb + k * 32), idesc,
+                        (r > 0 || k > 0) ? 1u : 0u);
+        tc_commit(&empty[stage]);
+        if (r == a.kpg - 1) tc_commit(&gfull[j & 1]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else {
+    // ---- converter / rescale warps ----
+    const int cw = warp - 2, hf = cw >> 2, quad = warp & 3;
+    const int row = quad * 32 + lane;               // TMEM lane = weight row of the tile
+    const int n = min(nt * BW + row, a.N - 1);
+    const uint32_t tl = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+    const int g0 = kb0 * BK / (a.kpg * BK);
+    const __half* srow = a.scales + static_cast<size_t>(n) * a.gpr + g0;
+    const __half* orow = a.offsets + static_cast<size_t>(n) * a.gpr + g0;
+    float acc[HC];
+#pragma unroll
+    for (int c = 0; c < HC; ++c) acc[c] = 0.f;
+    bool ok = true;
+    // group j's scale (kept for the rescale one group later) and (128 + z) as a bf16 pair;
+    // the raw values are loaded one group ahead so their latency hides behind a group's work
+    __half nsh = ngroups > 0 ? srow[0] : __half(), noh = ngroups > 0 ? orow[0] : __half();
+    auto group_params = [&](int j, float& sc, uint32_t& zz) {
+      sc = __half2float(nsh);
+      const float of = __half2float(noh);
+      if (j + 1 < ngroups) {
+        nsh = srow[j + 1];
+        noh = orow[j + 1];
+      }
+      const int z = sc != 0.f ? min(15, max(0, __float2int_rn(__fdividef(of, sc)))) : 0;
+      zz = (0x4300u | static_cast<uint32_t>(z)) * 0x10001u;
+    };
+    auto rescale = [&](int j, float sc) {
+      int go = 1;
+      if (!mbar_wait(&gfull[j & 1], (j >> 1) & 1, abort_flag)) {
+        record_error(a.err, kErrTimeoutTmemFull);
+        *abort_flag = 1;
+        go = 0;
+      }
+      go = __all_sync(0xffffffffu, go);
+      if (!go) return false;
+      tc_fence_after();
+      if constexpr (HC == 8) {
+        uint32_t v[8];
+        tmem_ld8(tl + (j & 1) * BT + hf * HC, v);
+        tc_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 8; ++c) acc[c] = fmaf(sc, __uint_as_float(v[c]), acc[c]);
+      } else {
+        uint32_t v[16];
+        tmem_ld16(tl + (j & 1) * BT + hf * HC, v);
+        tc_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 16; ++c) acc[c] = fmaf(sc, __uint_as_float(v[c]), acc[c]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&gempty[j & 1]);
+      return true;
+    };
+    int stage = 0;
+    uint32_t phase = 0;
+    float sc_cur = 0.f, sc_prev = 0.f;
+    uint32_t zz = 0x43004300u;
+    for (int kb = kb0; kb < kb1 && ok; ++kb) {
+      const int j = (kb - kb0) / a.kpg, r = (kb - kb0) % a.kpg;
+      if (r == 0) {
+        sc_prev = sc_cur;
+        group_params(j, sc_cur, zz);
+      }
+      int go = 1;
+      if (!mbar_wait(&full[stage], phase, abort_flag)) {
+        record_error(a.err, kErrTimeoutTmaFull);
+        *abort_flag = 1;
+        go = 0;
+      }
+      go = __all_sync(0xffffffffu, go);
+      if (!go) {
+        ok = false;
+        break;
+      }
+      // 16 packed bytes = elements [32 hf, 32 hf + 32) of this row's 64
+      const uint4 p = *reinterpret_cast<const uint4*>(sQ(stage) + row * 32 + hf * 16);
+      const uint32_t w[4] = {p.x, p.y, p.z, p.w};
+      uint32_t v[16];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          v[4 * c + i] = sub_bf16x2(((w[c] >> (4 * i)) & 0x000F000Fu) | 0x43004300u, zz);
+      tmem_st16(tl + ACOL + stage * 32 + hf * 16, v);
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ready[stage]);
+      if (r == a.kpg - 1 && j >= 1) ok = rescale(j - 1, sc_prev);
+      if (++stage == STAGES) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
+    if (ok && ngroups > 0) ok = rescale(ngroups - 1, sc_cur);
+    // running sums -> TMEM columns [0, BT) for the split-K exchange (every MMA has completed)
+    if (ok && ngroups > 0) {
+      uint32_t v[HC];
+#pragma unroll
+      for (int c = 0; c < HC; ++c) v[c] = __float_as_uint(acc[c]);
+      if constexpr (HC == 8) tmem_st8(tl + hf * HC, v);
+      else tmem_st16(tl + hf * HC, v);
+      tc_wait_st();
+    }
+    tc_fence_before();
+    if (threadIdx.x == 64) s_go[0] = (ngroups == 0) ? 2 : ((ok && !*abort_flag) ? 1 : 0);
+    named_bar_sync(2, NCONV * 32);
+    tc_fence_after();
+    if (hf == 0) {
+      // warps 2..5: the exchange of the cluster split-K (TMEM lane = quad * 32 + lane)
+      crs::publish<BT>(tl, s_go[0] == 1, sSlots, ws_tile, rank, S, quad * 32 + lane,
+                       threadIdx.x - 64);
+    }
+  }
+
+  tc_fence_before();
+  crs::sync_all();
+  tc_fence_after();
+  if (warp >= 2 && warp < 6) {
+    const int e = threadIdx.x - 64;
+    if (e == 0) crs::fetch<BT>(sSlots, ws_tile, rbar, rank, S);
+    const int x0 = a.mode == 1 ? nt * 64 : nt * BW;
+    auto epi = [&](int oc, int t0, int l, float4 (&accv)[crs::CW]) {
+      uint8_t* tile = crs::out_tile(sSlots, 0, oc);
+      crs::stage_out(a.mode, tile, l, accv, nullptr, 0, 0, 0);
+      crs::store_chunk(&tmC, tile, l, x0, t0);
+    };
+    const bool okr = crs::reduce<BT>(sSlots, rbar, rank, S, e, abort_flag, epi);
+    crs::store_wait(e & 31, false);
+    if (!okr) {
+      record_error(a.err, kErrTimeoutTmaFull);
+      *abort_flag = 1;
+      if (e == 0 && !mbar_wait(rbar, 0, nullptr, kWaitBudgetNs)) record_error(a.err, kErrTimeoutDrain);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace qs
+
 static PFN_cuTensorMapEncodeTiled_v12000 q_encode() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
@@ -345,6 +659,99 @@ static void launch_q(const CUtensorMap& tq, const CUtensorMap& tx, const CUtenso
   cfg.attrs = at;
   cfg.numAttrs = 1;
   C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, q::gemm_q_kernel<BT, STAGES, QBITS>, tq, tx, tc, a));
+}
+
+template <int BT>
+static void launch_qs(const CUtensorMap& tq, const CUtensorMap& tx, const CUtensorMap& tc,
+                      const qs::Args& a, int S, cudaStream_t st) {
+  constexpr int STAGES = 6;
+  using L = qs::Smem<BT, STAGES>;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(qs::gemm_qs_kernel<BT, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         L::TOTAL);
+    attr = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.n_tiles * S);
+  cfg.blockDim = dim3(qs::THREADS);
+  cfg.dynamicSmemBytes = L::TOTAL;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = S;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, qs::gemm_qs_kernel<BT, STAGES>, tq, tx, tc, a));
+}
+
+// Small-batch (M <= 32) GEMM for 4-bit weights whose offsets are integer multiples of the
+// scale (offset = z * s, z in 0..15: AWQ), group a multiple of 64.  Same operands as gemm_quant.
+void gemm_quant_iz(const at::Tensor& X, const at::Tensor& qw, const at::Tensor& scales,
+                   const at::Tensor& offsets, int64_t group, at::Tensor& C, int64_t mode,
+                   int64_t splits, at::Tensor& err, at::Tensor& ws) {
+  TORCH_CHECK(X.scalar_type() == at::kBFloat16 && X.stride(1) == 1, "gemm_quant_iz: X bf16");
+  TORCH_CHECK(qw.scalar_type() == at::kByte && qw.is_contiguous(), "gemm_quant_iz: packed uint8");
+  TORCH_CHECK(scales.scalar_type() == at::kHalf && offsets.scalar_type() == at::kHalf &&
+                  scales.is_contiguous() && offsets.is_contiguous(),
+              "gemm_quant_iz: contiguous fp16 scales / offsets");
+  const int M = X.size(0), K = X.size(1), N = qw.size(0);
+  TORCH_CHECK(M <= 32, "gemm_quant_iz: at most 32 rows");
+  TORCH_CHECK(qw.size(1) * 2 == K, "gemm_quant_iz: 4-bit packed width");
+  TORCH_CHECK(group >= 64 && group % 64 == 0 && K % group == 0, "gemm_quant_iz: group % 64");
+  TORCH_CHECK(scales.size(0) == N && scales.size(1) == K / group, "gemm_quant_iz: scales shape");
+  if (M == 0) return;
+  const int BT = M <= 16 ? 16 : 32;
+  qs::Args a = {};
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.n_tiles = (N + 127) / 128;
+  a.kb_total = K / 64;
+  a.kpg = group / 64;
+  a.gpr = K / group;
+  const int ngroups = a.gpr;
+  int S = static_cast<int>(splits);
+  if (S <= 0) {
+    // two CTAs per SM (TMEM: 256 columns each); at least two groups per split
+    int nsm = 148;
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, X.get_device());
+    S = 1;
+    for (int s = 2; s <= 8; ++s)
+      if (a.n_tiles * s <= 2 * nsm && ngroups / s >= 2) S = s;
+  }
+  S = std::max(1, std::min(S, std::min(8, ngroups)));
+  while (S > 1 && ws.numel() < crs::ws_floats(a.n_tiles, BT, S)) --S;
+  const int gps = (ngroups + S - 1) / S;
+  a.kb_per_split = gps * a.kpg;
+  a.ws = S > 1 ? ws.data_ptr<float>() : nullptr;
+  a.scales = reinterpret_cast<const __half*>(scales.data_ptr());
+  a.offsets = reinterpret_cast<const __half*>(offsets.data_ptr());
+  a.mode = mode;
+  a.err = err.data_ptr<int>();
+  const bool vec_ok = (reinterpret_cast<uintptr_t>(C.data_ptr()) % 16 == 0) && (C.stride(0) % 4 == 0);
+  if (mode == 1) TORCH_CHECK(N % 128 == 0 && vec_ok, "gemm_quant_iz swiglu layout");
+  CUtensorMap tq;
+  {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(qw.size(1)), static_cast<cuuint64_t>(N)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(qw.stride(0))};
+    cuuint32_t box[2] = {32, 128};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = q_encode()(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, qw.data_ptr(), dims, strides,
+                            box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    TORCH_CHECK(r == CUDA_SUCCESS, "gemm_quant_iz: tensor map");
+  }
+  const CUtensorMap tx = make_tmap_bf16_2d(X.data_ptr(), K, M, X.stride(0) * 2, 64, BT,
+                                           CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tc;
+  TORCH_CHECK(make_tmap_out(C, mode, M, N, crs::out_box_rows(BT, S), &tc),
+              "gemm_quant_iz: C must be 16-byte aligned with a 16-byte multiple row stride");
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (BT == 16) launch_qs<16>(tq, tx, tc, a, S, st);
+  else launch_qs<32>(tq, tx, tc, a, S, st);
 }
 
 // X [M, K] bf16; qw [N, K*bits/8] uint8; scales / offsets [N, K/group] fp16.

@@ -434,7 +434,8 @@ class ModelRunner:
         if fwd:
             ops.forward_tokens(d_ids[:num_decode], d_src, self.d_last_out)
         cu_list = cu_q.tolist()
-        ts, tr = prefill_tiles(cu_list, num_decode, self.model.group)
+        ts, tr = prefill_tiles(cu_list, num_decode, self.model.group,
+                               block_size=self.block_size, head_dim=self.model.d)
         tiles = torch.tensor([ts, tr], dtype=torch.int32).to(self.device, non_blocking=True) \
             if ts else None
         max_len = int(seq_lens.max()) if B else 1

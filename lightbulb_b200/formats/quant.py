@@ -32,6 +32,9 @@ class QuantWeight:
     offsets: torch.Tensor  # [N, K / group] fp16
     bits: int
     group: int
+    # offsets are integer multiples of the scales (offset = z * s, z in 0..15: AWQ zero points),
+    # which lets small batches use the integer-weight kernel (per-group rescale after the MMA)
+    int_zero: bool = False
 
     @property
     def shape(self):
@@ -43,22 +46,23 @@ class QuantWeight:
 
     def to(self, device=None, dtype=None) -> "QuantWeight":
         return QuantWeight(self.qw.to(device), self.scales.to(device), self.offsets.to(device),
-                           self.bits, self.group)
+                           self.bits, self.group, self.int_zero)
 
     def contiguous(self) -> "QuantWeight":
         return QuantWeight(self.qw.contiguous(), self.scales.contiguous(),
-                           self.offsets.contiguous(), self.bits, self.group)
+                           self.offsets.contiguous(), self.bits, self.group, self.int_zero)
 
     def rows(self, idx) -> "QuantWeight":
         return QuantWeight(self.qw[idx], self.scales[idx], self.offsets[idx], self.bits,
-                           self.group)
+                           self.group, self.int_zero)
 
     def cols(self, k0: int, k1: int) -> "QuantWeight":
         assert k0 % self.group == 0 and k1 % self.group == 0 and k0 % 64 == 0
         b = self.bits
         return QuantWeight(self.qw[:, k0 * b // 8:k1 * b // 8],
                            self.scales[:, k0 // self.group:k1 // self.group],
-                           self.offsets[:, k0 // self.group:k1 // self.group], b, self.group)
+                           self.offsets[:, k0 // self.group:k1 // self.group], b, self.group,
+                           self.int_zero)
 
     def pad_head_rows(self, n_heads: int, d: int, dp: int) -> "QuantWeight":
         """Insert all-zero rows (q = 0, scale = offset = 0 -> w = 0) after each head's d rows."""
@@ -70,7 +74,7 @@ class QuantWeight:
             out[:, :d] = t.reshape((n_heads, d) + tuple(t.shape[1:]))
             return out.reshape((n_heads * dp,) + tuple(t.shape[1:]))
         return QuantWeight(pad(self.qw), pad(self.scales), pad(self.offsets), self.bits,
-                           self.group)
+                           self.group, self.int_zero)
 
     def unpack(self) -> torch.Tensor:
         """Integer values [N, K] (int16)."""
@@ -113,7 +117,7 @@ def cat_rows(ws) -> QuantWeight:
     b, g = ws[0].bits, ws[0].group
     assert all(w.bits == b and w.group == g for w in ws)
     return QuantWeight(torch.cat([w.qw for w in ws]), torch.cat([w.scales for w in ws]),
-                       torch.cat([w.offsets for w in ws]), b, g)
+                       torch.cat([w.offsets for w in ws]), b, g, all(w.int_zero for w in ws))
 
 
 def interleave_rows(gate: QuantWeight, up: QuantWeight, group_rows: int = 64) -> QuantWeight:
@@ -132,7 +136,8 @@ def from_awq(q: torch.Tensor, z: torch.Tensor, s: torch.Tensor, group: int) -> Q
     """q [N, K] 0..15, z [N, K/g] 0..15, s [N, K/g]."""
     qw = pack4(q)
     sf = s.float()
-    return QuantWeight(qw, sf.to(torch.float16), (z.float() * sf).to(torch.float16), 4, group)
+    return QuantWeight(qw, sf.to(torch.float16), (z.float() * sf).to(torch.float16), 4, group,
+                       int_zero=True)
 
 
 def from_q8_0(raw: np.ndarray, n: int, k: int) -> QuantWeight:

@@ -78,8 +78,13 @@ class ForwardBatch:
         return self.input_ids.shape[0]
 
 
-def prefill_tiles(cu_q: List[int], first_seq: int, group: int, rows_per_tile: int = 64):
-    """Work list for the prefill attention kernel: (seq, first packed row) per CTA."""
+def prefill_tiles(cu_q: List[int], first_seq: int, group: int,
+                  rows_per_tile: Optional[int] = None, block_size: int = 16,
+                  head_dim: int = 128):
+    """Work list for the prefill attention kernel: (seq, first packed row) per CTA, with the
+    tile height of the kernel that ``ops.paged_attention`` selects for this geometry."""
+    if rows_per_tile is None:
+        rows_per_tile = ops.prefill_rows_per_tile(group, block_size, head_dim)
     seqs, rows = [], []
     for s in range(first_seq, len(cu_q) - 1):
         n = (cu_q[s + 1] - cu_q[s]) * group

@@ -316,7 +316,7 @@ def random_packed_awq_model(cfg: ModelConfig, seed: int = 0, rank: int = 0, worl
         qw = torch.randint(0, 256, (n, k // 2), generator=g, device=device, dtype=torch.int32)
         s = torch.empty(n, k // group, device=device).uniform_(0.001, 0.02, generator=g)
         z = torch.randint(0, 16, (n, k // group), generator=g, device=device).float()
-        return QuantWeight(qw.to(torch.uint8), s.half(), (z * s).half(), 4, group)
+        return QuantWeight(qw.to(torch.uint8), s.half(), (z * s).half(), 4, group, int_zero=True)
 
     for i in range(cfg.num_layers):
         p = f"model.layers.{i}."

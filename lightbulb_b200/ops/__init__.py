@@ -190,6 +190,14 @@ def gemm_pair(a: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = No
     return out
 
 
+def use_int_zero_kernel(w) -> bool:
+    """Small batches of 4-bit weights with integer zero points (AWQ) run on the integer-weight
+    kernel (``gemm_quant_iz``: weights exact in tensor memory, scale applied per group after
+    the MMA); ``LB_QUANT_IZ=0`` keeps them on the full-dequant kernel."""
+    return (getattr(w, "int_zero", False) and w.bits == 4 and w.group % 64 == 0
+            and _os.environ.get("LB_QUANT_IZ", "1") != "0")
+
+
 def gemm_quant(a: torch.Tensor, w, out: Optional[torch.Tensor] = None, mode: int = EPI_STORE,
                splits: int = 0) -> torch.Tensor:
     """``a @ dequant(w).T`` for a :class:`~lightbulb_b200.formats.quant.QuantWeight`."""
@@ -203,8 +211,12 @@ def gemm_quant(a: torch.Tensor, w, out: Optional[torch.Tensor] = None, mode: int
             out = torch.empty(m, n, dtype=torch.bfloat16, device=a.device)
     if a.is_cuda:
         sc = scratch(a.device)
-        _need_c().gemm_quant(a, w.qw, w.scales, w.offsets, w.bits, w.group, out, mode,
-                             max(0, splits), sc.err, sc.gemm_ws)
+        if m <= 32 and use_int_zero_kernel(w):
+            _need_c().gemm_quant_iz(a, w.qw, w.scales, w.offsets, w.group, out, mode,
+                                    max(0, splits), sc.err, sc.gemm_ws)
+        else:
+            _need_c().gemm_quant(a, w.qw, w.scales, w.offsets, w.bits, w.group, out, mode,
+                                 max(0, splits), sc.err, sc.gemm_ws)
         _launches[0] += 1
         return out
     return gemm(a, w.dequantize(torch.bfloat16), out, None, mode)
@@ -325,6 +337,20 @@ def decode_splits(num_seqs: int, num_kv_heads: int, max_kv_len: int, sms: int = 
     return max(1, min(32, (slots + ctas - 1) // ctas, max(1, max_kv_len // 512)))
 
 
+_PREFILL_IMPL = _os.environ.get("LB_PREFILL_ATTN", "tc")
+
+
+def prefill_rows_per_tile(group: int, block_size: int = 16, head_dim: int = 128) -> int:
+    """Packed query rows per CTA of the prefill / verify attention kernel that will run for
+    this geometry: 128 for the tcgen05 kernel (block size 16, head dim 128, power-of-two GQA
+    group <= 16; ``LB_PREFILL_ATTN=fa2`` selects the mma.sync kernel), 64 otherwise.  The
+    work list (``models.llama.prefill_tiles``) must be built with the same value."""
+    if (_PREFILL_IMPL == "tc" and block_size == 16 and head_dim == 128 and 1 <= group <= 16
+            and group & (group - 1) == 0):
+        return 128
+    return 64
+
+
 def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                     block_tables: torch.Tensor, seq_lens: torch.Tensor, cu_q: torch.Tensor,
                     out: torch.Tensor, group: int, decode: bool,
@@ -347,6 +373,12 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
             C.paged_decode_tma(q, k_cache, v_cache, out, block_tables, seq_lens, group, scale,
                                num_splits, po, pl, scratch(q.device).err)
             _launches[0] += 2 if num_splits > 1 else 1
+            return out
+        if not decode and prefill_rows_per_tile(group, k_cache.shape[2], d) == 128:
+            C.paged_attention_tc(q, k_cache, v_cache, out, block_tables, seq_lens, cu_q,
+                                 tile_seq, tile_row0, group, scale, causal,
+                                 scratch(q.device).err)
+            _launches[0] += 1
             return out
         C.paged_attention(q, k_cache, v_cache, out, block_tables, seq_lens, cu_q, tile_seq,
                           tile_row0, group, scale, decode, num_splits, po, pl, causal,

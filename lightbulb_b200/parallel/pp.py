@@ -116,7 +116,8 @@ class PipelineEngine:
         dev = self.device
         tiles = None
         if not decode:
-            ts, tr = prefill_tiles(slots, 0, self.model.group)
+            ts, tr = prefill_tiles(slots, 0, self.model.group, head_dim=self.model.d,
+                                   block_size=self.bs)
             tiles = (torch.tensor(ts, dtype=torch.int32, device=dev),
                      torch.tensor(tr, dtype=torch.int32, device=dev))
         return ForwardBatch(

@@ -125,7 +125,8 @@ def bench_gemm_quant(m, n, k, kind="awq", iters=20):
     for _ in range(copies):
         qw = torch.randint(0, 256, (n, k * bits // 8), device="cuda", dtype=torch.int32)
         sc = torch.rand(n, k // group, device="cuda").half() * 0.01
-        ws.append(QuantWeight(qw.to(torch.uint8), sc, sc * 8, bits, group))
+        ws.append(QuantWeight(qw.to(torch.uint8), sc, sc * 8, bits, group,
+                              int_zero=kind == "awq"))
     a = torch.randn(m, k, device="cuda").to(torch.bfloat16)
     it = [0]
 

@@ -215,6 +215,80 @@ def test_paged_prefill_chunked(hq, hkv):
     assert _rel(out.cpu(), ref) < 2e-2
 
 
+@pytest.mark.parametrize("hq,hkv", [(32, 8), (16, 1), (32, 2), (2, 2)])
+@pytest.mark.parametrize("causal", [True, False])
+def test_paged_prefill_tcgen05(hq, hkv, causal):
+    """tcgen05 prefill / verify attention (S and O in TMEM, P from TMEM) against the fp32
+    reference: chunked tails, a 4k context (many key tiles, the running-max rescale), ragged
+    lengths around the 16-key block and 128-key tile edges, and verify-shaped 5-token chunks."""
+    from lightbulb_b200.models.llama import prefill_tiles
+    G = hq // hkv
+    assert ops.prefill_rows_per_tile(G) == 128
+    seq_lens = [5, 127, 129, 700, 4096, 300, 300, 2050]
+    q_lens = [5, 100, 129, 512, 384, 5, 5, 33]
+    q, kc, vc, bt, sl, cu = _paged_setup(seq_lens, q_lens, hq, hkv, seed=11)
+    q = q * 4     # sharper softmax: later tiles raise the row max past the rescale threshold
+    if causal:
+        ref = _ref_paged(q, kc, vc, bt, sl, cu)
+    else:
+        outs = []
+        for i in range(len(seq_lens)):
+            L = int(sl[i])
+            q0, q1 = int(cu[i]), int(cu[i + 1])
+            nb = (L + 15) // 16
+            blk = bt[i, :nb].long()
+            k = kc[blk].permute(0, 2, 1, 3).reshape(nb * 16, hkv, -1)[:L]
+            v = vc[blk].permute(0, 2, 1, 3).reshape(nb * 16, hkv, -1)[:L]
+            outs.append(attention_ref(q[q0:q1], k, v, torch.arange(L - (q1 - q0), L),
+                                      torch.arange(L), causal=False))
+        ref = torch.cat(outs, 0)
+    ts, tr = prefill_tiles(cu.tolist(), 0, G)
+    assert all(r % 128 == 0 for r in tr)
+    out = torch.full(q.shape, float("nan"), dtype=torch.bfloat16, device=DEV)
+    ops.paged_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), sl.to(DEV), cu.to(DEV),
+                        out, G, decode=False, causal=causal,
+                        tile_seq=torch.tensor(ts, dtype=torch.int32, device=DEV),
+                        tile_row0=torch.tensor(tr, dtype=torch.int32, device=DEV))
+    torch.cuda.synchronize()
+    ops.check_errors()
+    assert torch.isfinite(out.float()).all()
+    assert _rel(out.cpu(), ref) < 2e-2
+
+
+def test_paged_prefill_tcgen05_strided_q_matches_fa2():
+    """q read straight out of a fused QKV buffer (row stride > Hq * 128): the tcgen05 kernel and
+    the mma.sync kernel give the same result."""
+    from lightbulb_b200 import _C
+    from lightbulb_b200.models.llama import prefill_tiles
+    hq, hkv = 32, 8
+    seq_lens, q_lens = [1000, 64], [256, 64]
+    q, kc, vc, bt, sl, cu = _paged_setup(seq_lens, q_lens, hq, hkv, seed=5)
+    T = q.shape[0]
+    qkv = torch.randn(T, (hq + 2 * hkv) * 128).to(torch.bfloat16)
+    qkv[:, :hq * 128] = q.reshape(T, -1)
+    qv = qkv.to(DEV)[:, :hq * 128].view(T, hq, 128)
+    args = (kc.to(DEV), vc.to(DEV))
+    outs = []
+    for rows in (128, 64):
+        ts, tr = prefill_tiles(cu.tolist(), 0, 4, rows_per_tile=rows)
+        o = torch.empty(T, hq, 128, dtype=torch.bfloat16, device=DEV)
+        tsd = torch.tensor(ts, dtype=torch.int32, device=DEV)
+        trd = torch.tensor(tr, dtype=torch.int32, device=DEV)
+        if rows == 128:
+            _C.paged_attention_tc(qv, *args, o, bt.to(DEV), sl.to(DEV), cu.to(DEV), tsd, trd, 4,
+                                  1.0 / 128 ** 0.5, True, ops.scratch(qv.device).err)
+        else:
+            _C.paged_attention(qv, *args, o, bt.to(DEV), sl.to(DEV), cu.to(DEV), tsd, trd, 4,
+                               1.0 / 128 ** 0.5, False, 1, None, None, True,
+                               ops.scratch(qv.device).err)
+        outs.append(o)
+    torch.cuda.synchronize()
+    ops.check_errors()
+    ref = _ref_paged(q, kc, vc, bt, sl, cu)
+    assert _rel(outs[0].cpu(), ref) < 2e-2
+    assert _rel(outs[0].cpu(), outs[1].cpu()) < 2e-2
+
+
 def test_sampling_greedy_and_topk_topp():
     from lightbulb_b200.engine.sampling import sample_row_reference
     torch.manual_seed(0)
