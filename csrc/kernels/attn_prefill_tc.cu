@@ -41,18 +41,20 @@ CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t inner, uint64_t outer,
 namespace fa {
 
 constexpr int D = 128;          // head dim
-constexpr int BM = 128;         // packed query rows per CTA
+constexpr int QT = 2;           // query tiles of 128 packed rows per CTA (ping-pong)
+constexpr int BM = 128 * QT;    // packed query rows per CTA
 constexpr int BN = 128;         // keys per tile
 constexpr int BS = 16;          // paged block size
-constexpr int THREADS = 192;
+constexpr int THREADS = 64 + QT * 128;
 constexpr int HALF = BN * 128;  // one 64-dim half of a 128-row tile (bytes)
 constexpr int TILE = 2 * HALF;  // 32 KB
-constexpr int KV_STAGES = 2;
-constexpr int SMEM_Q = 0;
-constexpr int SMEM_KV = TILE;                        // [stage][K tile | V tile]
-constexpr int SMEM_BAR = SMEM_KV + KV_STAGES * 2 * TILE;
+constexpr int KST = 2, VST = 2;
+constexpr int SMEM_Q = 0;                            // [QT] tiles
+constexpr int SMEM_K = QT * TILE;                    // [KST]
+constexpr int SMEM_V = SMEM_K + KST * TILE;          // [VST]
+constexpr int SMEM_BAR = SMEM_V + VST * TILE;
 constexpr int SMEM_TOTAL = SMEM_BAR + 256 + 1024;    // + alignment slack
-constexpr uint32_t TMEM_COLS = 512, COL_O = 0, COL_S = 128;
+constexpr uint32_t TMEM_COLS = 512;                  // O_t at 128 t, S_t at 256 + 128 t
 constexpr float RESCALE_THRESHOLD = 8.f;              // log2 units: P <= 2^8 between rescales
 
 struct Args {
@@ -99,18 +101,19 @@ __global__ void __launch_bounds__(THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint8_t* sQ = smem + SMEM_Q;
-  auto sK = [&](int s) { return smem + SMEM_KV + s * 2 * TILE; };
-  auto sV = [&](int s) { return smem + SMEM_KV + s * 2 * TILE + TILE; };
+  auto sQ = [&](int t) { return smem + SMEM_Q + t * TILE; };
+  auto sK = [&](int s) { return smem + SMEM_K + s * TILE; };
+  auto sV = [&](int s) { return smem + SMEM_V + s * TILE; };
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SMEM_BAR);
-  uint64_t* q_full = bars;            // TMA Q
-  uint64_t* kv_full = bars + 1;       // [2] TMA K/V stage
-  uint64_t* kv_empty = bars + 3;      // [2] P V of the stage done
-  uint64_t* s_full = bars + 5;        // [2] S_j computed
-  uint64_t* p_ready = bars + 7;       // [2] P_j in TMEM (4 softmax warps)
-  uint64_t* pv_done = bars + 9;       // every P V completion
-  uint64_t* o_full = bars + 10;       // last P V done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  uint64_t* q_full = bars;                 // TMA Q (both tiles)
+  uint64_t* k_full = bars + 1;             // [KST]
+  uint64_t* k_empty = k_full + KST;        // [KST] S of every query tile done
+  uint64_t* v_full = k_empty + KST;        // [VST]
+  uint64_t* v_empty = v_full + VST;        // [VST] P V of every query tile done
+  uint64_t* s_full = v_empty + VST;        // [QT] S_t of the current key tile (and all earlier MMAs)
+  uint64_t* p_ready = s_full + QT;         // [QT] P_t in TMEM (4 softmax warps)
+  uint64_t* o_full = p_ready + QT;         // last P V done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -118,13 +121,18 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
-      mbar_init(&s_full[s], 1);
-      mbar_init(&p_ready[s], 4);
+    for (int s = 0; s < KST; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
     }
-    mbar_init(pv_done, 1);
+    for (int s = 0; s < VST; ++s) {
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int t = 0; t < QT; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_ready[t], 4);
+    }
     mbar_init(o_full, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -152,8 +160,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int q_len = a.cu_q[seq + 1] - q_start;
   const int kv_len = a.seq_lens[seq];
   const int nrows_seq = q_len << a.log2g;
+  const int nqt = row0 + 128 < nrows_seq ? QT : 1;   // query tiles holding valid rows
   const int* btab = a.block_tables + static_cast<size_t>(seq) * a.bt_stride;
-  // keys this tile needs: causal rows see keys <= kv_len - q_len + token
+  // keys this CTA needs: causal rows see keys <= kv_len - q_len + token
   int k_limit = kv_len;
   if (a.causal) {
     const int last_row = min(row0 + BM, nrows_seq) - 1;
@@ -163,24 +172,20 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int seq_blocks = (kv_len + BS - 1) / BS;
 
   // producer bookkeeping for the drain on abort: parity of the last load issued per stage
-  int issued_par[KV_STAGES] = {-1, -1};
+  int k_par[KST] = {-1, -1}, v_par[VST] = {-1, -1};
   bool q_issued = false;
   if (warp == 0) {
     if (lane == 0 && ntiles > 0) {
       const uint64_t pol = policy_evict_last();
-      mbar_arrive_expect_tx(q_full, TILE);
+      mbar_arrive_expect_tx(q_full, nqt * TILE);
       q_issued = true;
-      const int tok0 = q_start + (row0 >> a.log2g);
-      for (int h = 0; h < 2; ++h) tma_load_3d_q(sQ + h * HALF, &tmQ, q_full, h * 64, kvh * a.group, tok0);
-      int stage = 0;
-      uint32_t phase = 0;
-      for (int j = 0; j < ntiles; ++j) {
-        if (!mbar_wait(&kv_empty[stage], phase ^ 1u, abort_flag)) {
-          record_error(a.err, kErrTimeoutSmemEmpty);
-          *abort_flag = 1;
-          break;
-        }
-        mbar_arrive_expect_tx(&kv_full[stage], 2 * TILE);
+      for (int t = 0; t < nqt; ++t) {
+        const int tok0 = q_start + ((row0 + 128 * t) >> a.log2g);
+        for (int h = 0; h < 2; ++h)
+          tma_load_3d_q(sQ(t) + h * HALF, &tmQ, q_full, h * 64, kvh * a.group, tok0);
+      }
+      auto load_tile = [&](const CUtensorMap* tm, uint8_t* dst, uint64_t* bar, int j) {
+        mbar_arrive_expect_tx(bar, TILE);
         for (int b = 0; b < BN / BS; ++b) {
           const int lb = j * (BN / BS) + b;
           int blk = lb < seq_blocks ? btab[lb] : 0;
@@ -189,63 +194,77 @@ __global__ void __launch_bounds__(THREADS, 1)
             blk = 0;
           }
           const int row = (blk * a.num_kv_heads + kvh) * BS;
-          for (int h = 0; h < 2; ++h) {
-            tma_load_2d(sK(stage) + h * HALF + b * BS * 128, &tmK, &kv_full[stage], h * 64, row, pol);
-            tma_load_2d(sV(stage) + h * HALF + b * BS * 128, &tmV, &kv_full[stage], h * 64, row, pol);
-          }
+          for (int h = 0; h < 2; ++h) tma_load_2d(dst + h * HALF + b * BS * 128, tm, bar, h * 64, row, pol);
         }
-        issued_par[stage] = static_cast<int>(phase);
-        if (++stage == KV_STAGES) {
-          stage = 0;
-          phase ^= 1u;
+      };
+      for (int j = 0; j < ntiles; ++j) {
+        const int ks = j % KST, vs = j % VST;
+        if (!mbar_wait(&k_empty[ks], ((j / KST) & 1) ^ 1u, abort_flag)) {
+          record_error(a.err, kErrTimeoutSmemEmpty);
+          *abort_flag = 1;
+          break;
         }
+        load_tile(&tmK, sK(ks), &k_full[ks], j);
+        k_par[ks] = (j / KST) & 1;
+        if (!mbar_wait(&v_empty[vs], ((j / VST) & 1) ^ 1u, abort_flag)) {
+          record_error(a.err, kErrTimeoutSmemEmpty);
+          *abort_flag = 1;
+          break;
+        }
+        load_tile(&tmV, sV(vs), &v_full[vs], j);
+        v_par[vs] = (j / VST) & 1;
       }
     }
   } else if (warp == 1) {
     if (lane == 0 && ntiles > 0) {
-      constexpr uint32_t idesc_s = idesc_bf16_f32(BM, BN);
-      constexpr uint32_t idesc_o = idesc_bf16_f32(BM, D, 0, 1);  // B (V) MN-major
+      constexpr uint32_t idesc_s = idesc_bf16_f32(128, BN);
+      constexpr uint32_t idesc_o = idesc_bf16_f32(128, D, 0, 1);  // B (V) MN-major
       bool ok = mbar_wait(q_full, 0, abort_flag);
-      if (!ok) {
-        record_error(a.err, kErrTimeoutTmaFull);
-        *abort_flag = 1;
-      }
-      const uint32_t qb = smem_u32(sQ);
-      auto issue_s = [&](int j) {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_full[st], (j >> 1) & 1, abort_flag)) return false;
+      // O_t += P_t V_j  (P_t over S_t in TMEM)
+      auto issue_pv = [&](int t, int j) {
+        if (!mbar_wait(&p_ready[t], j & 1, abort_flag)) return false;
         tc_fence_after();
-        const uint32_t kb = smem_u32(sK(st));
-        const uint32_t sc = tmem_base + COL_S + st * 128;
+        const uint32_t vb = smem_u32(sV(j % VST));
+        const uint32_t pc = tmem_base + 256 + 128 * t;
+#pragma unroll
+        for (int k = 0; k < BN / 16; ++k)
+          tc_mma_f16_ts(tmem_base + 128 * t, pc + k * 8, sw128_mnmajor_desc(vb + k * 16 * 128, HALF),
+                        idesc_o, (j > 0 || k > 0) ? 1u : 0u);
+        return true;
+      };
+      // S_t = Q_t K_j^T
+      auto issue_s = [&](int t, int j) {
+        const uint32_t qb = smem_u32(sQ(t)), kb = smem_u32(sK(j % KST));
+        const uint32_t sc = tmem_base + 256 + 128 * t;
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
           const uint32_t off = (k >> 2) * HALF + (k & 3) * 32;
           tc_mma_f16(sc, sw128_kmajor_desc(qb + off), sw128_kmajor_desc(kb + off), idesc_s,
                      k > 0 ? 1u : 0u);
         }
-        tc_commit(&s_full[st]);
-        return true;
+        tc_commit(&s_full[t]);  // arrives once this and every earlier MMA have completed
       };
-      auto issue_pv = [&](int j) {
-        const int st = j & 1;
-        if (!mbar_wait(&p_ready[st], (j >> 1) & 1, abort_flag)) return false;
-        tc_fence_after();
-        const uint32_t vb = smem_u32(sV(st));
-        const uint32_t pc = tmem_base + COL_S + st * 128;
-#pragma unroll
-        for (int k = 0; k < BN / 16; ++k)
-          tc_mma_f16_ts(tmem_base + COL_O, pc + k * 8, sw128_mnmajor_desc(vb + k * 16 * 128, HALF),
-                        idesc_o, (j > 0 || k > 0) ? 1u : 0u);
-        tc_commit(&kv_empty[st]);
-        tc_commit(pv_done);
-        return true;
-      };
-      if (ok) ok = issue_s(0);
       for (int j = 0; ok && j < ntiles; ++j) {
-        if (j + 1 < ntiles) ok = issue_s(j + 1);
-        if (ok) ok = issue_pv(j);
+        ok = mbar_wait(&k_full[j % KST], (j / KST) & 1, abort_flag);
+        if (ok && j > 0) ok = mbar_wait(&v_full[(j - 1) % VST], ((j - 1) / VST) & 1, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        for (int t = 0; t < nqt && ok; ++t) {
+          // the previous tile's P V runs first: S_t is written over P_t, in issue order
+          if (j > 0) ok = issue_pv(t, j - 1);
+          if (ok) issue_s(t, j);
+        }
+        if (!ok) break;
+        tc_commit(&k_empty[j % KST]);
+        if (j > 0) tc_commit(&v_empty[(j - 1) % VST]);
+      }
+      if (ok) ok = mbar_wait(&v_full[(ntiles - 1) % VST], ((ntiles - 1) / VST) & 1, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        for (int t = 0; t < nqt && ok; ++t) ok = issue_pv(t, ntiles - 1);
       }
       if (ok) {
+        tc_commit(&v_empty[(ntiles - 1) % VST]);
         tc_commit(o_full);
       } else {
         record_error(a.err, kErrTimeoutTmaFull);
@@ -253,20 +272,21 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   } else {
-    // ---- softmax / epilogue: thread = query row (TMEM lane quad * 32 + lane) ----
+    // ---- softmax / epilogue: warpgroup t = query tile t, thread = query row (TMEM lane) ----
+    const int t = (warp - 2) >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
-    const int pr = row0 + r;
+    const int pr = row0 + 128 * t + r;
     const bool valid_row = pr < nrows_seq;
     const int tok = pr >> a.log2g;
     const int qpos = kv_len - q_len + tok;
     const int klim = !valid_row ? 0 : (a.causal ? min(kv_len, qpos + 1) : kv_len);
     const uint32_t tl = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+    const uint32_t colO = 128 * t, colS = 256 + 128 * t;
     float m_used = -INFINITY, l = 0.f;
-    bool ok = true;
+    bool ok = t < nqt;
     for (int j = 0; j < ntiles && ok; ++j) {
-      const int st = j & 1;
-      int go = mbar_wait(&s_full[st], (j >> 1) & 1, abort_flag) ? 1 : 0;
+      int go = mbar_wait(&s_full[t], j & 1, abort_flag) ? 1 : 0;
       go = __all_sync(0xffffffffu, go);
       if (!go) {
         if (lane == 0) record_error(a.err, kErrTimeoutTmemFull);
@@ -278,10 +298,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t sr[128];
 #pragma unroll
       for (int c = 0; c < 4; ++c)
-        tmem_ld32(tl + COL_S + st * 128 + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(sr + 32 * c));
+        tmem_ld32(tl + colS + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(sr + 32 * c));
       tc_wait_ld();
-      const int key0 = j * BN;
-      const int nvalid = min(BN, max(0, klim - key0));  // keys [key0, key0 + nvalid) visible
+      const int nvalid = min(BN, max(0, klim - j * BN));  // keys [j BN, j BN + nvalid) visible
       float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 128; ++c) {
@@ -291,29 +310,19 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       const bool need = mx > m_used + RESCALE_THRESHOLD;
       const float m_new = need ? mx : m_used;
+      // s_full's arrival implies the previous P V into O_t has completed (issue order)
       if (__any_sync(0xffffffffu, need) && j > 0) {
-        // rescale O (rows that moved their max) once the previous P V has landed in it
-        int g2 = mbar_wait(pv_done, (j - 1) & 1, abort_flag) ? 1 : 0;
-        g2 = __all_sync(0xffffffffu, g2);
-        if (!g2) {
-          if (lane == 0) record_error(a.err, kErrTimeoutTmemFull);
-          *abort_flag = 1;
-          ok = false;
-          break;
-        }
-        tc_fence_after();
         const float corr = need ? exp2f(m_used - m_new) : 1.f;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t ov[32];
-          tmem_ld32(tl + COL_O + 32 * c, ov);
+          tmem_ld32(tl + colO + 32 * c, ov);
           tc_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * corr);
-          tmem_st16(tl + COL_O + 32 * c, *reinterpret_cast<uint32_t(*)[16]>(ov));
-          tmem_st16(tl + COL_O + 32 * c + 16, *reinterpret_cast<uint32_t(*)[16]>(ov + 16));
+          tmem_st16(tl + colO + 32 * c, *reinterpret_cast<uint32_t(*)[16]>(ov));
+          tmem_st16(tl + colO + 32 * c + 16, *reinterpret_cast<uint32_t(*)[16]>(ov + 16));
         }
-        tc_wait_st();
       }
       if (need) {
         l *= exp2f(m_used - m_new);  // 0 when m_used = -inf
@@ -330,13 +339,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
 #pragma unroll
       for (int c = 0; c < 4; ++c)
-        tmem_st16(tl + COL_S + st * 128 + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(pk + 16 * c));
+        tmem_st16(tl + colS + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(pk + 16 * c));
       tc_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_ready[st]);
+      if (lane == 0) mbar_arrive(&p_ready[t]);
     }
-    // ---- epilogue: O / l -> out[token][head][:] ----
+    // ---- epilogue: O_t / l -> out[token][head][:] ----
     if (ok && ntiles > 0) {
       int go = mbar_wait(o_full, 0, abort_flag) ? 1 : 0;
       go = __all_sync(0xffffffffu, go);
@@ -348,7 +357,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t ov[32];
-          tmem_ld32(tl + COL_O + 32 * c, ov);
+          tmem_ld32(tl + colO + 32 * c, ov);
           tc_wait_ld();
           if (valid_row) {
 #pragma unroll
@@ -373,9 +382,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   if (warp == 0 && lane == 0 && *abort_flag) {
     bool drained = !q_issued || mbar_wait(q_full, 0, nullptr, kWaitBudgetNs);
-    for (int s = 0; s < KV_STAGES; ++s)
-      if (issued_par[s] >= 0)
-        drained &= mbar_wait(&kv_full[s], static_cast<uint32_t>(issued_par[s]), nullptr, kWaitBudgetNs);
+    for (int s = 0; s < KST; ++s)
+      if (k_par[s] >= 0) drained &= mbar_wait(&k_full[s], static_cast<uint32_t>(k_par[s]), nullptr, kWaitBudgetNs);
+    for (int s = 0; s < VST; ++s)
+      if (v_par[s] >= 0) drained &= mbar_wait(&v_full[s], static_cast<uint32_t>(v_par[s]), nullptr, kWaitBudgetNs);
     if (!drained) record_error(a.err, kErrTimeoutDrain);
   }
   tc_fence_before();
@@ -406,7 +416,7 @@ bool prefill_tc_supported(int64_t group, int64_t block_size, int64_t head_dim) {
 }
 
 // q [T, Hq, 128] (row stride 16-byte aligned), caches [num_blocks, Hkv, 16, 128]; the work list
-// (tile_seq, tile_row0) has one entry per 128 packed rows of each sequence.
+// (tile_seq, tile_row0) has one entry per 256 packed rows of each sequence.
 void paged_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                         at::Tensor& out, const at::Tensor& block_tables, const at::Tensor& seq_lens,
                         const at::Tensor& cu_q, const at::Tensor& tile_seq,
@@ -454,7 +464,7 @@ void paged_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, const at
     cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(Hq),
                           static_cast<cuuint64_t>(T)};
     cuuint64_t strides[2] = {static_cast<cuuint64_t>(D * 2), static_cast<cuuint64_t>(q.stride(0) * 2)};
-    cuuint32_t box[3] = {64, static_cast<cuuint32_t>(group), static_cast<cuuint32_t>(BM / group)};
+    cuuint32_t box[3] = {64, static_cast<cuuint32_t>(group), static_cast<cuuint32_t>(128 / group)};
     cuuint32_t es[3] = {1, 1, 1};
     CUresult r = fa_encode()(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, q.data_ptr(), dims, strides,
                              box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,

@@ -342,12 +342,13 @@ _PREFILL_IMPL = _os.environ.get("LB_PREFILL_ATTN", "tc")
 
 def prefill_rows_per_tile(group: int, block_size: int = 16, head_dim: int = 128) -> int:
     """Packed query rows per CTA of the prefill / verify attention kernel that will run for
-    this geometry: 128 for the tcgen05 kernel (block size 16, head dim 128, power-of-two GQA
-    group <= 16; ``LB_PREFILL_ATTN=fa2`` selects the mma.sync kernel), 64 otherwise.  The
-    work list (``models.llama.prefill_tiles``) must be built with the same value."""
+    this geometry: 256 for the tcgen05 kernel (two 128-row query tiles; block size 16, head
+    dim 128, power-of-two GQA group <= 16; ``LB_PREFILL_ATTN=fa2`` selects the mma.sync
+    kernel), 64 otherwise.  The work list (``models.llama.prefill_tiles``) must be built with
+    the same value."""
     if (_PREFILL_IMPL == "tc" and block_size == 16 and head_dim == 128 and 1 <= group <= 16
             and group & (group - 1) == 0):
-        return 128
+        return 256
     return 64
 
 
@@ -374,7 +375,7 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
                                num_splits, po, pl, scratch(q.device).err)
             _launches[0] += 2 if num_splits > 1 else 1
             return out
-        if not decode and prefill_rows_per_tile(group, k_cache.shape[2], d) == 128:
+        if not decode and prefill_rows_per_tile(group, k_cache.shape[2], d) == 256:
             C.paged_attention_tc(q, k_cache, v_cache, out, block_tables, seq_lens, cu_q,
                                  tile_seq, tile_row0, group, scale, causal,
                                  scratch(q.device).err)

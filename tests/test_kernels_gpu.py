@@ -223,7 +223,7 @@ def test_paged_prefill_tcgen05(hq, hkv, causal):
     lengths around the 16-key block and 128-key tile edges, and verify-shaped 5-token chunks."""
     from lightbulb_b200.models.llama import prefill_tiles
     G = hq // hkv
-    assert ops.prefill_rows_per_tile(G) == 128
+    assert ops.prefill_rows_per_tile(G) == 256
     seq_lens = [5, 127, 129, 700, 4096, 300, 300, 2050]
     q_lens = [5, 100, 129, 512, 384, 5, 5, 33]
     q, kc, vc, bt, sl, cu = _paged_setup(seq_lens, q_lens, hq, hkv, seed=11)
@@ -243,7 +243,7 @@ def test_paged_prefill_tcgen05(hq, hkv, causal):
                                       torch.arange(L), causal=False))
         ref = torch.cat(outs, 0)
     ts, tr = prefill_tiles(cu.tolist(), 0, G)
-    assert all(r % 128 == 0 for r in tr)
+    assert all(r % 256 == 0 for r in tr)
     out = torch.full(q.shape, float("nan"), dtype=torch.bfloat16, device=DEV)
     ops.paged_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), sl.to(DEV), cu.to(DEV),
                         out, G, decode=False, causal=causal,
@@ -269,12 +269,12 @@ def test_paged_prefill_tcgen05_strided_q_matches_fa2():
     qv = qkv.to(DEV)[:, :hq * 128].view(T, hq, 128)
     args = (kc.to(DEV), vc.to(DEV))
     outs = []
-    for rows in (128, 64):
+    for rows in (256, 64):
         ts, tr = prefill_tiles(cu.tolist(), 0, 4, rows_per_tile=rows)
         o = torch.empty(T, hq, 128, dtype=torch.bfloat16, device=DEV)
         tsd = torch.tensor(ts, dtype=torch.int32, device=DEV)
         trd = torch.tensor(tr, dtype=torch.int32, device=DEV)
-        if rows == 128:
+        if rows == 256:
             _C.paged_attention_tc(qv, *args, o, bt.to(DEV), sl.to(DEV), cu.to(DEV), tsd, trd, 4,
                                   1.0 / 128 ** 0.5, True, ops.scratch(qv.device).err)
         else:
