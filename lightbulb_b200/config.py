@@ -264,6 +264,7 @@ class ServerConfig:
     tls_cert: Optional[str] = None
     tls_key: Optional[str] = None
     tls_self_signed: bool = False
+    tls_acme: Optional[object] = None      # server.tls.AcmeConfig
 
     @classmethod
     def from_env(cls) -> "ServerConfig":
@@ -276,4 +277,6 @@ class ServerConfig:
         c.tls_cert = os.environ.get("LIGHTBULB_TLS_CERT")
         c.tls_key = os.environ.get("LIGHTBULB_TLS_KEY")
         c.tls_self_signed = os.environ.get("LIGHTBULB_TLS_SELF_SIGNED", "0") == "1"
+        from .server.tls import AcmeConfig
+        c.tls_acme = AcmeConfig.from_env()
         return c

@@ -105,7 +105,8 @@ def create_app(state: Optional[AppState] = None) -> FastAPI:
         t0 = time.perf_counter()
         path = request.url.path
         key_hash = None
-        if state.auth.enabled and path not in ("/health",):
+        open_path = path == "/health" or path.startswith("/.well-known/acme-challenge/")
+        if state.auth.enabled and not open_path:
             h = request.headers.get("authorization", "")
             if not h.lower().startswith("bearer "):
                 return _err(401, "missing bearer API key", "authentication_error")
@@ -118,7 +119,7 @@ def create_app(state: Optional[AppState] = None) -> FastAPI:
             if not state.auth.hit(key_hash, limit):
                 return _err(429, "rate limit exceeded", "rate_limit_error")
         resp = await call_next(request)
-        if state.auth.enabled and path != "/health":
+        if state.auth.enabled and not open_path:
             state.auth.audit(key_hash, request.method, path, resp.status_code,
                              (time.perf_counter() - t0) * 1e3)
         return resp
@@ -131,6 +132,14 @@ def create_app(state: Optional[AppState] = None) -> FastAPI:
                             content={"status": "ok" if ok else "unhealthy",
                                      "model_loaded": state.engine is not None,
                                      "error": None if ok else state.engine.last_error})
+
+    @app.get("/.well-known/acme-challenge/{token}")
+    async def acme_challenge(token: str):
+        from .tls import CHALLENGES
+        ka = CHALLENGES.get(token)
+        if ka is None:
+            return PlainTextResponse("Challenge not found", status_code=404)
+        return PlainTextResponse(ka)
 
     @app.get("/metrics")
     async def metrics():

@@ -1,6 +1,7 @@
 """HTTP API tests without a socket (httpx ASGI transport) over a tiny CPU engine."""
 import asyncio
 import json
+import os
 
 import httpx
 import pytest
@@ -209,3 +210,42 @@ def test_async_engine_releases_finished_requests(engine):
     import time
     time.sleep(0.2)
     assert not [r for r, s in engine.engine.seqs.items() if s.finished]
+
+
+def test_acme_config_cached_certificate_fallback_and_challenge(tmp_path, monkeypatch):
+    """ACME (reference src/tls.rs:252-300,387-450): configuration from the environment, a valid
+    cached pair is used as is, otherwise a self-signed fallback for the first domain; HTTP-01
+    challenge tokens are served without authentication."""
+    from cryptography import x509
+    from cryptography.x509.oid import NameOID
+    from lightbulb_b200.config import ServerConfig
+    from lightbulb_b200.server import tls
+    monkeypatch.setenv("LIGHTBULB_TLS_ACME_DOMAINS", "example.test, www.example.test")
+    monkeypatch.setenv("LIGHTBULB_TLS_ACME_EMAIL", "ops@example.test")
+    monkeypatch.setenv("LIGHTBULB_TLS_ACME_CERT_DIR", str(tmp_path / "acme"))
+    sc = ServerConfig.from_env()
+    assert sc.tls_acme.domains == ["example.test", "www.example.test"]
+    kw = tls.ssl_kwargs(sc)
+    with open(kw["ssl_certfile"], "rb") as f:
+        c = x509.load_pem_x509_certificate(f.read())
+    assert c.subject.get_attributes_for_oid(NameOID.COMMON_NAME)[0].value == "example.test"
+    # a valid cached ACME pair takes precedence over the fallback
+    cert, key = tls.self_signed(str(tmp_path / "issued"), common_name="example.test")
+    os.makedirs(tmp_path / "acme", exist_ok=True)
+    os.replace(cert, tmp_path / "acme" / "acme_cert.pem")
+    os.replace(key, tmp_path / "acme" / "acme_key.pem")
+    assert tls.ssl_kwargs(sc)["ssl_certfile"] == str(tmp_path / "acme" / "acme_cert.pem")
+    st = AppState(database_url="sqlite://:memory:")      # auth on: challenges stay open
+    assert st.auth.enabled
+    tls.CHALLENGES.add("tok123", "tok123.thumbprint")
+
+    async def go():
+        async with _client(st) as c:
+            r = await c.get("/.well-known/acme-challenge/tok123")
+            assert r.status_code == 200 and r.text == "tok123.thumbprint"
+            r = await c.get("/.well-known/acme-challenge/other")
+            assert r.status_code == 404
+    try:
+        run(go())
+    finally:
+        tls.CHALLENGES.remove("tok123")
