@@ -301,13 +301,17 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_ld32(tl + colS + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(sr + 32 * c));
       tc_wait_ld();
       const int nvalid = min(BN, max(0, klim - j * BN));  // keys [j BN, j BN + nvalid) visible
-      float mx = -INFINITY;
+      // raw scores: masked keys -> -inf (only tiles that cross a row's limit); the softmax scale
+      // (> 0, order preserving) is applied to the max and folded into the exponent's FMA
+      if (!__all_sync(0xffffffffu, nvalid >= BN)) {
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        const float x = c < nvalid ? __uint_as_float(sr[c]) * a.scale_log2 : -INFINITY;
-        sr[c] = __float_as_uint(x);
-        mx = fmaxf(mx, x);
+        for (int c = 0; c < 128; ++c)
+          if (c >= nvalid) sr[c] = __float_as_uint(-INFINITY);
       }
+      float mr = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) mr = fmaxf(mr, __uint_as_float(sr[c]));
+      const float mx = mr * a.scale_log2;
       const bool need = mx > m_used + RESCALE_THRESHOLD;
       const float m_new = need ? mx : m_used;
       // s_full's arrival implies the previous P V into O_t has completed (issue order)
@@ -329,11 +333,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         m_used = m_new;
       }
       const float ms = m_used == -INFINITY ? 0.f : m_used;
+      const float sc = a.scale_log2;
       uint32_t pk[64];
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
-        const float p0 = exp2f(__uint_as_float(sr[2 * c]) - ms);
-        const float p1 = exp2f(__uint_as_float(sr[2 * c + 1]) - ms);
+        const float p0 = exp2f(fmaf(__uint_as_float(sr[2 * c]), sc, -ms));
+        const float p1 = exp2f(fmaf(__uint_as_float(sr[2 * c + 1]), sc, -ms));
         l += p0 + p1;
         pk[c] = pack_bf16x2(p0, p1);
       }

@@ -186,8 +186,16 @@ __global__ void __launch_bounds__(THREADS) rowpar_norm_kernel(const Args a) {
       const int64_t nv = static_cast<int64_t>(rows_of(j, a.T, rp)) * HV;
       const uint4* src = a.partial + static_cast<int64_t>(j) * rp * HV;
       uint4* dst = a.recv1[j] + (static_cast<int64_t>(par) * W + me) * src_stride;
-#pragma unroll 4
-      for (int64_t v = first; v < nv; v += step) dst[v] = canon4(src[v]);
+      // four loads in flight before their peer stores (the stores do not alias the partial)
+      int64_t v = first;
+      for (; v + 3 * step < nv; v += 4 * step) {
+        uint4 t[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) t[u] = src[v + u * step];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) dst[v + u * step] = canon4(t[u]);
+      }
+      for (; v < nv; v += step) dst[v] = canon4(src[v]);
     }
   }
 
@@ -207,14 +215,32 @@ __global__ void __launch_bounds__(THREADS) rowpar_norm_kernel(const Args a) {
       float acc[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-      for (int s = 0; s < W; ++s) {
-        uint4 q = zero;
-        if (s == me) {
-          q = a.partial != nullptr ? a.partial[(row0 + i) * HV + vi] : r1[me * src_stride + off];
-        } else if (ok) {
+      // one load of every source's slot in flight at once; only slots that are not yet
+      // written are polled again (a chain of dependent polls would cost one memory latency
+      // per source)
+      uint4 qs[MAX_WORLD];
+#pragma unroll
+      for (int s = 0; s < MAX_WORLD; ++s) {
+        if (s >= W) continue;
+        if (s == me)
+          qs[s] = a.partial != nullptr ? a.partial[(row0 + i) * HV + vi] : r1[me * src_stride + off];
+        else
+          qs[s] = ld_vol(r1 + s * src_stride + off);
+      }
+#pragma unroll
+      for (int s = 0; s < MAX_WORLD; ++s) {
+        if (s >= W) continue;
+        uint4 q = qs[s];
+        if (s != me) {
           uint4* p = r1 + s * src_stride + off;
-          if (poll(p, q, t0)) *p = sent;
-          else { ok = false; q = zero; }
+          if (!ok) {
+            q = zero;
+          } else if (lanes_ready(q) || poll(p, q, t0)) {
+            *p = sent;
+          } else {
+            ok = false;
+            q = zero;
+          }
         }
         float f[8];
         unpack8(q, f);
@@ -272,17 +298,38 @@ __global__ void __launch_bounds__(THREADS) rowpar_norm_kernel(const Args a) {
     uint4* r2 = a.recv2[me] + static_cast<int64_t>(par) * a.t_max * HV;
     const int64_t step = static_cast<int64_t>(gridDim.x) * THREADS;
     const int64_t first = static_cast<int64_t>(blockIdx.x) * THREADS + threadIdx.x;
+    // up to GB vectors of this thread: loads issued together, then polled where still unwritten
+    constexpr int GB = 8;
+    int64_t idx[GB];
+    uint4 xs[GB];
+    int n = 0;
+    auto flush = [&]() {
+#pragma unroll
+      for (int u = 0; u < GB; ++u)
+        if (u < n) xs[u] = ld_vol(r2 + idx[u]);
+#pragma unroll
+      for (int u = 0; u < GB; ++u) {
+        if (u >= n || !ok) continue;
+        uint4 x = xs[u];
+        if (!lanes_ready(x) && !poll(r2 + idx[u], x, t0)) {
+          ok = false;
+          continue;
+        }
+        r2[idx[u]] = sent;
+        a.h[idx[u]] = x;
+      }
+      n = 0;
+    };
     for (int d = 1; d < W && ok; ++d) {
       const int j = (me + d) % W;
       const int64_t base = static_cast<int64_t>(j) * rp * HV;
       const int64_t nv = static_cast<int64_t>(rows_of(j, a.T, rp)) * HV;
       for (int64_t v = first; v < nv; v += step) {
-        uint4 x;
-        if (!poll(r2 + base + v, x, t0)) { ok = false; break; }
-        r2[base + v] = sent;
-        a.h[base + v] = x;
+        idx[n++] = base + v;
+        if (n == GB) flush();
       }
     }
+    if (ok && n > 0) flush();
   }
   if (!ok) record_error(a.err, kErrTimeoutPeer);
   if (tr) tr[3] = globaltimer_ns();
