@@ -70,6 +70,8 @@ def parse():
     ap.add_argument("--prefix-len", type=int, default=1024)
     ap.add_argument("--chunk", type=int, default=512)
     ap.add_argument("--spec-k", type=int, default=4)
+    ap.add_argument("--spec-fallback", dest="spec_no_fallback", action="store_false",
+                    help="spec config: keep the engine's auto-fallback to plain decoding")
     ap.add_argument("--h2o-budget", type=int, default=2048)
     ap.add_argument("--h2o-sinks", type=int, default=4)
     ap.add_argument("--block-size", type=int, default=16)
@@ -576,7 +578,11 @@ def bench_spec(args):
     packed = random_packed_model(mcfg, seed=args.seed, rank=rank, world=world, device=dev)
     eng = LLMEngine(ecfg, packed, None, comm=comm, tp_rank=rank, tp_size=world)
     dpacked = random_packed_model(dcfg, seed=args.seed + 7, rank=rank, world=world, device=dev)
-    spec = eng.attach_draft(dpacked, dcfg, k=k, num_blocks=nb)
+    # the engine's auto-fallback (off below an acceptance of 0.3 after 10 rounds) stays off
+    # here, so every timed step is a speculative round: unrelated random-init models accept
+    # almost nothing, and the number shows the cost of the draft + verify machinery
+    spec = eng.attach_draft(dpacked, dcfg, k=k, num_blocks=nb,
+                            min_acceptance=0.0 if args.spec_no_fallback else 0.3)
     load_s = time.perf_counter() - t0
     prompts = _prompts(args, min(mcfg.vocab_size, dcfg.vocab_size))
     out_len = max(args.output_len, 8)
@@ -627,6 +633,7 @@ def bench_spec(args):
                    "l2": "inputs larger than L2 (weights + KV per step)"},
         "acceptance_rate": round(acc / prop, 4) if prop else None,
         "speculation_active": spec.active, "spec_rounds": spec.stats.rounds,
+        "auto_fallback": not args.spec_no_fallback,
         "e2e": {"value": round(tokens / wall, 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": None, "d2h_bytes_per_step": None,
                 "api": "LLMEngine.step() with SpeculativeDecoder attached"},

@@ -989,6 +989,23 @@ static void launch_bt(const CUtensorMap& tw, const CUtensorMap& tx, const GemmAr
                          L::TOTAL);
     attr = true;
   }
+  if (a.sk_q > 0) {
+    // Stream-K: a tile's finisher waits for the partials of CTAs with higher indices, so every
+    // CTA must be resident at once -- a cooperative launch guarantees it (or fails loudly)
+    // instead of relying on an idle GPU.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = L::TOTAL;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeCooperative;
+    at[0].val.cooperative = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BT, STAGES>, tw, tx, a));
+    return;
+  }
   C10_CUDA_CHECK(launch_k(gemm_tc_kernel<BT, STAGES>, dim3(grid), dim3(kThreads), L::TOTAL, st,
                           nullptr, 0, tw, tx, a));
 }

@@ -156,26 +156,47 @@ class SpeculativeDecoder:
             so.cow_pairs = []
         t0 = time.perf_counter()
         # ---- draft: catch up, then k proposals ------------------------------------
+        # Proposal j + 1 takes proposal j as its input token straight from the device (the
+        # runner's token forwarding), so the k draft steps launch back to back; each step's ids
+        # are read on the host one step later, while the next step runs.  The draft block
+        # manager keeps no prefix index, so placeholder ids stand in for tokens not yet read.
         props: Dict[int, List[int]] = {s.seq_id: [] for s in seqs}
         for s in seqs:
             self._draft_register(s)
+        row_of: Dict[int, int] = {}            # seq_id -> row of the previous step's samples
+        pending = None                         # (PendingTokens, seq_ids in row order)
+
+        def collect(p):
+            if p is not None:
+                for sid, t in zip(p[1], p[0].tokens()):
+                    props[sid].append(t)
+
         for step in range(k):
-            chunks = []
+            chunks, src = [], []
             for s in seqs:
-                toks = s.all_token_ids + props[s.seq_id]
+                sid = s.seq_id
+                toks = s.all_token_ids + [0] * step
                 dv = _SeqView(s, toks, len(toks) - s.prompt_len)
-                start = self.draft_len[s.seq_id]
+                start = self.draft_len[sid]
                 n = len(toks) - start
-                slots, cow = self.dbm.append_slots(s.seq_id, n, toks[start:])
+                slots, cow = self.dbm.append_slots(sid, n, toks[start:])
                 if cow:
                     self.draft.kv.copy_blocks(cow)
                 chunks.append(ScheduledChunk(dv, start, n, slots, True))
-                self.draft_len[s.seq_id] = len(toks)
-            dec = [c for c in chunks if c.num_tokens == 1]
-            pre = [c for c in chunks if c.num_tokens > 1]
-            res = self.draft.execute(SchedulerOutput(decode=dec, prefill=pre))
-            for c, t in zip(res.chunks, res.tokens):
-                props[c.seq.seq_id].append(t)
+                src.append(row_of[sid] if step > 0 else -1)
+                self.draft_len[sid] = len(toks)
+            if step == 0:
+                dec = [c for c in chunks if c.num_tokens == 1]
+                pre = [c for c in chunks if c.num_tokens > 1]
+                res = self.draft.execute(SchedulerOutput(decode=dec, prefill=pre), defer=True)
+            else:
+                res = self.draft.execute(SchedulerOutput(decode=chunks, prefill=[]),
+                                         src_rows=src, defer=True)
+            collect(pending)
+            order = [c.seq.seq_id for c in res.chunks]
+            row_of = {sid: i for i, sid in enumerate(order)}
+            pending = (res.pending, order)
+        collect(pending)
         t1 = time.perf_counter()
         # ---- target verify: k+1 tokens per sequence, every row sampled -------------
         vchunks = []
