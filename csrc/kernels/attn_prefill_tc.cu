@@ -86,6 +86,38 @@ __device__ __forceinline__ uint64_t sw128_mnmajor_desc(uint32_t saddr, uint32_t 
   return d;
 }
 
+// Softmax arithmetic on the packed and multi-input forms of sm_100: a 3-input max, fp32 pairs
+// (fma / add .f32x2: two lanes per instruction) and the hardware base-2 exponential
+// (ex2.approx, denormal results flushed: P is rounded to bf16 anyway).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t pack_f2(float lo, float hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+__device__ __forceinline__ void unpack_f2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma_f2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add_f2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ void tma_load_3d_q(void* dst, const CUtensorMap* tmap, uint64_t* bar,
                                               int c0, int c1, int c2) {
   asm volatile(
@@ -310,7 +342,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       float mr = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 128; ++c) mr = fmaxf(mr, __uint_as_float(sr[c]));
+      for (int c = 0; c < 128; c += 2)
+        mr = max3f(mr, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
       const float mx = mr * a.scale_log2;
       const bool need = mx > m_used + RESCALE_THRESHOLD;
       const float m_new = need ? mx : m_used;
@@ -333,18 +366,30 @@ __global__ void __launch_bounds__(THREADS, 1)
         m_used = m_new;
       }
       const float ms = m_used == -INFINITY ? 0.f : m_used;
-      const float sc = a.scale_log2;
-      uint32_t pk[64];
+      const uint64_t sc2 = pack_f2(a.scale_log2, a.scale_log2), nms2 = pack_f2(-ms, -ms);
+      uint64_t l2 = pack_f2(0.f, 0.f);
+      // P in 32-key chunks, each stored to TMEM as soon as it is packed (P chunk q overwrites
+      // S columns [16 q, 16 q + 16), whose scores are already in registers)
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float p0 = exp2f(fmaf(__uint_as_float(sr[2 * c]), sc, -ms));
-        const float p1 = exp2f(fmaf(__uint_as_float(sr[2 * c + 1]), sc, -ms));
-        l += p0 + p1;
-        pk[c] = pack_bf16x2(p0, p1);
+      for (int q = 0; q < 4; ++q) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const int e = 32 * q + 2 * c;
+          float x0, x1;
+          unpack_f2(fma_f2(pack_f2(__uint_as_float(sr[e]), __uint_as_float(sr[e + 1])), sc2,
+                           nms2), x0, x1);
+          const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+          l2 = add_f2(l2, pack_f2(p0, p1));
+          pk[c] = pack_bf16x2(p0, p1);
+        }
+        tmem_st16(tl + colS + 16 * q, pk);
       }
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-        tmem_st16(tl + colS + 16 * c, *reinterpret_cast<uint32_t(*)[16]>(pk + 16 * c));
+      {
+        float la, lb;
+        unpack_f2(l2, la, lb);
+        l += la + lb;
+      }
       tc_wait_st();
       tc_fence_before();
       __syncwarp();
