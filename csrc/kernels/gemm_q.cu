@@ -22,6 +22,9 @@
 #include <cudaTypedefs.h>
 #include <torch/extension.h>
 
+#include <cstdlib>
+#include <string>
+
 #include "cluster_rs.cuh"
 #include "common.cuh"
 
@@ -341,10 +344,13 @@ struct Args {
   float* ws;
 };
 
-template <int BT, int STAGES>
+// HK: 64-element halves per k-block (1 or 2).  With HK = 2 every TMA row request of the packed
+// tile moves 64 bytes instead of 32.
+template <int BT, int STAGES, int HK>
 struct Smem {
-  static constexpr int X_BYTES = BT * BK * 2;       // 1024-aligned (BT = 16 / 32)
-  static constexpr int Q_BYTES = BW * BK / 2;       // packed 4-bit tile
+  static constexpr int X_HALF = BT * BK * 2;        // one 64-column SW128 activation tile
+  static constexpr int X_BYTES = HK * X_HALF;       // 1024-aligned (BT = 16 / 32)
+  static constexpr int Q_BYTES = BW * BK * HK / 2;  // packed 4-bit tile
   static constexpr int STAGE = X_BYTES + Q_BYTES;
   static constexpr int PIPE = STAGES * STAGE;
   static constexpr int SLOTS = crs::smem_bytes(BT, 8);
@@ -359,13 +365,14 @@ __device__ __forceinline__ uint32_t sub_bf16x2(uint32_t a, uint32_t b) {
   return d;
 }
 
-template <int BT, int STAGES>
+template <int BT, int STAGES, int HK>
 __global__ void __launch_bounds__(THREADS, 2)
     gemm_qs_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmX,
                    const __grid_constant__ CUtensorMap tmC, const Args a) {
-  using L = Smem<BT, STAGES>;
+  using L = Smem<BT, STAGES, HK>;
+  constexpr int AW = 32 * HK;  // TMEM columns of one weight stage (2 bf16 per column)
   constexpr int HC = BT / 2;  // token columns per converter half
-  static_assert(ACOL >= 2 * BT && ACOL + STAGES * 32 <= TMEM_COLS, "TMEM plan");
+  static_assert(ACOL >= 2 * BT && ACOL + STAGES * AW <= TMEM_COLS, "TMEM plan");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -430,8 +437,9 @@ __global__ void __launch_bounds__(THREADS, 2)
           break;
         }
         mbar_arrive_expect_tx(&full[stage], L::Q_BYTES + L::X_BYTES);
-        tma_load_2d(sQ(stage), &tmQ, &full[stage], kb * BK / 2, nt * BW, pw);
-        tma_load_2d(sX(stage), &tmX, &full[stage], kb * BK, 0, px);
+        tma_load_2d(sQ(stage), &tmQ, &full[stage], kb * BK * HK / 2, nt * BW, pw);
+        for (int h = 0; h < HK; ++h)
+          tma_load_2d(sX(stage) + h * L::X_HALF, &tmX, &full[stage], (kb * HK + h) * BK, 0, px);
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1u;
@@ -458,11 +466,11 @@ __global__ void __launch_bounds__(THREADS, 2)
         tc_fence_after();
         const uint32_t xb = smem_u32(sX(stage));
         const uint32_t acc = tmem_base + (j & 1) * BT;
-        const uint32_t at = tmem_base + ACOL + stage * 32;
+        const uint32_t at = tmem_base + ACOL + stage * AW;
 #pragma unroll
-        for (int k = 0; k < BK / 16; ++k)
-          tc_mma_f16_ts(acc, at + k * 8, sw128_kmajor_desc(xb + k * 32), idesc,
-                        (r > 0 || k > 0) ? 1u : 0u);
+        for (int k = 0; k < HK * BK / 16; ++k)
+          tc_mma_f16_ts(acc, at + k * 8, sw128_kmajor_desc(xb + (k >> 2) * L::X_HALF + (k & 3) * 32),
+                        idesc, (r > 0 || k > 0) ? 1u : 0u);
         tc_commit(&empty[stage]);
         if (r == a.kpg - 1) tc_commit(&gfull[j & 1]);
         if (++stage == STAGES) {
@@ -546,16 +554,19 @@ __global__ void __launch_bounds__(THREADS, 2)
         ok = false;
         break;
       }
-      // 16 packed bytes = elements [32 hf, 32 hf + 32) of this row's 64
-      const uint4 p = *reinterpret_cast<const uint4*>(sQ(stage) + row * 32 + hf * 16);
-      const uint32_t w[4] = {p.x, p.y, p.z, p.w};
-      uint32_t v[16];
+      // 16 HK packed bytes = elements [32 HK hf, 32 HK (hf + 1)) of this row's 64 HK
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+      for (int u = 0; u < HK; ++u) {
+        const uint4 p = *reinterpret_cast<const uint4*>(sQ(stage) + row * 32 * HK + (hf * HK + u) * 16);
+        const uint32_t w[4] = {p.x, p.y, p.z, p.w};
+        uint32_t v[16];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          v[4 * c + i] = sub_bf16x2(((w[c] >> (4 * i)) & 0x000F000Fu) | 0x43004300u, zz);
-      tmem_st16(tl + ACOL + stage * 32 + hf * 16, v);
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            v[4 * c + i] = sub_bf16x2(((w[c] >> (4 * i)) & 0x000F000Fu) | 0x43004300u, zz);
+        tmem_st16(tl + ACOL + stage * AW + (hf * HK + u) * 16, v);
+      }
       tc_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -661,14 +672,14 @@ static void launch_q(const CUtensorMap& tq, const CUtensorMap& tx, const CUtenso
   C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, q::gemm_q_kernel<BT, STAGES, QBITS>, tq, tx, tc, a));
 }
 
-template <int BT>
+template <int BT, int HK>
 static void launch_qs(const CUtensorMap& tq, const CUtensorMap& tx, const CUtensorMap& tc,
                       const qs::Args& a, int S, cudaStream_t st) {
-  constexpr int STAGES = 6;
-  using L = qs::Smem<BT, STAGES>;
+  constexpr int STAGES = HK == 1 ? 6 : 3;  // TMEM: weight stages of 32 HK columns after 64
+  using L = qs::Smem<BT, STAGES, HK>;
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(qs::gemm_qs_kernel<BT, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(qs::gemm_qs_kernel<BT, STAGES, HK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          L::TOTAL);
     attr = true;
   }
@@ -684,7 +695,7 @@ static void launch_qs(const CUtensorMap& tq, const CUtensorMap& tx, const CUtens
   at[0].val.clusterDim.z = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, qs::gemm_qs_kernel<BT, STAGES>, tq, tx, tc, a));
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, qs::gemm_qs_kernel<BT, STAGES, HK>, tq, tx, tc, a));
 }
 
 // Small-batch (M <= 32) GEMM for 4-bit weights whose offsets are integer multiples of the
@@ -709,8 +720,14 @@ void gemm_quant_iz(const at::Tensor& X, const at::Tensor& qw, const at::Tensor& 
   a.N = N;
   a.K = K;
   a.n_tiles = (N + 127) / 128;
-  a.kb_total = K / 64;
-  a.kpg = group / 64;
+  // 128-element k-blocks (64-byte rows per TMA request) when the groups allow it
+  static const bool wide_ok = []() {
+    const char* e = std::getenv("LB_QS_BK");
+    return !(e != nullptr && std::string(e) == "64");
+  }();
+  const int HK = (wide_ok && group % 128 == 0) ? 2 : 1;
+  a.kb_total = K / (64 * HK);
+  a.kpg = group / (64 * HK);
   a.gpr = K / group;
   const int ngroups = a.gpr;
   int S = static_cast<int>(splits);
@@ -737,7 +754,7 @@ void gemm_quant_iz(const at::Tensor& X, const at::Tensor& qw, const at::Tensor& 
   {
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(qw.size(1)), static_cast<cuuint64_t>(N)};
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(qw.stride(0))};
-    cuuint32_t box[2] = {32, 128};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(32 * HK), 128};
     cuuint32_t es[2] = {1, 1};
     CUresult r = q_encode()(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, qw.data_ptr(), dims, strides,
                             box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -750,8 +767,13 @@ void gemm_quant_iz(const at::Tensor& X, const at::Tensor& qw, const at::Tensor& 
   TORCH_CHECK(make_tmap_out(C, mode, M, N, crs::out_box_rows(BT, S), &tc),
               "gemm_quant_iz: C must be 16-byte aligned with a 16-byte multiple row stride");
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  if (BT == 16) launch_qs<16>(tq, tx, tc, a, S, st);
-  else launch_qs<32>(tq, tx, tc, a, S, st);
+  if (HK == 2) {
+    if (BT == 16) launch_qs<16, 2>(tq, tx, tc, a, S, st);
+    else launch_qs<32, 2>(tq, tx, tc, a, S, st);
+  } else {
+    if (BT == 16) launch_qs<16, 1>(tq, tx, tc, a, S, st);
+    else launch_qs<32, 1>(tq, tx, tc, a, S, st);
+  }
 }
 
 // X [M, K] bf16; qw [N, K*bits/8] uint8; scales / offsets [N, K/group] fp16.
